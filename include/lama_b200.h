@@ -1,0 +1,142 @@
+/*
+ * lama_b200.h - C ABI of the B200 big-lama inpainting engine.
+ *
+ * The engine runs the big-lama FFC-ResNet generator forward pass on one
+ * NVIDIA B200 (sm_100a).  It is the drop-in replacement for the reference
+ * engine's operator boundary:
+ *
+ *   infer(store, plan, input: Vec<f32> [4][h][w], h, w, args) -> Result<Vec<f32> [3][h][w], String>
+ *       lama-rs/src/main.rs:318-361
+ *   cuda::run(store, model, &input, h, w) -> Result<Vec<f32>, String>
+ *       lama-rs/src/cuda.rs:1542-1691
+ *   WeightStore::open + cuda::load_steps
+ *       lama-rs/src/weights.rs:80-106, lama-rs/src/cuda.rs:903-962
+ *
+ * Conventions (same as the reference):
+ *   - buffers are owned by the caller; the engine never keeps a pointer past
+ *     the call that received it;
+ *   - the network input is [4][h][w] float, NCHW: RGB * (1 - mask), then the
+ *     mask (0 or 1); h and w are multiples of 8 (main.rs:241-242);
+ *   - the network output is [3][h][w] float, the sigmoid output before
+ *     compositing;
+ *   - every function returns 0 on success and a negative LAMA_E* code on
+ *     failure; lama_last_error() gives the message (the reference's
+ *     `Err(String)`).  There is no CPU fallback: a GPU failure is an error.
+ *
+ * Threading: an engine is bound to one device and is not thread-safe; engines
+ * on different devices may be driven concurrently from different threads.
+ *
+ * Arithmetic: the reference is FP32.  Convolutions run on the tensor core as
+ * three BF16 products of split operands (x = hi + lo) with FP32 accumulation,
+ * which tracks FP32 to ~1e-5 relative per layer; transforms run in FP32.
+ */
+#ifndef LAMA_B200_H
+#define LAMA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct lama_engine lama_engine;
+
+enum {
+  LAMA_OK = 0,
+  LAMA_EINVAL = -1,   /* bad argument (size not a multiple of 8, null pointer, ...) */
+  LAMA_EWEIGHTS = -2, /* weight file missing, truncated, not F32, wrong shape */
+  LAMA_ECUDA = -3,    /* CUDA runtime / driver error */
+  LAMA_EDEVICE = -4,  /* a kernel reported a device-side error (timeout, bad plan) */
+  LAMA_ENOMEM = -5,   /* device allocation refused */
+  LAMA_EUNSUPPORTED = -6
+};
+
+/* Open the safetensors weight file and build the engine on CUDA device
+ * `device`.  Replaces WeightStore::open (weights.rs:80-106: every tensor must
+ * be F32 and inside the file) and cuda::load_steps (cuda.rs:903-962: BN
+ * folding, weight upload).  On failure *out is still set when possible so
+ * that lama_last_error() can report; close it with lama_close(). */
+int lama_open(const char* weights_path, int device, lama_engine** out);
+
+/* Forward pass on host buffers: in = [batch][4][h][w], out = [batch][3][h][w].
+ * Replaces cuda::run (cuda.rs:1542-1691) / infer (main.rs:318-361); batch > 1
+ * runs independent images in one pass. */
+int lama_forward(lama_engine* e, const float* in, int batch, int h, int w, float* out);
+
+/* Same with device pointers (inputs already in device memory), ordered on
+ * the engine's stream; returns after the work is queued. */
+int lama_forward_device(lama_engine* e, const float* d_in, int batch, int h, int w, float* d_out);
+
+/* build_input + forward + composite on host u8 buffers: rgb [batch][h][w][3],
+ * mask [batch][h][w] (non-zero = hole), out_rgb [batch][h][w][3].  Any h, w
+ * >= 1: the network runs at the next multiple of 8 with reflect extension
+ * (main.rs:175-196, 241-242); masked pixels take round(clamp(v,0,1)*255)
+ * and every other byte is copied from rgb (main.rs:272-307). */
+int lama_inpaint_u8(lama_engine* e, const uint8_t* rgb, const uint8_t* mask, int batch, int h, int w,
+                    uint8_t* out_rgb);
+
+/* Same with device pointers, ordered on the engine's stream. */
+int lama_inpaint_u8_device(lama_engine* e, const uint8_t* d_rgb, const uint8_t* d_mask, int batch, int h, int w,
+                           uint8_t* d_out_rgb);
+
+/* The FFC resblock stack alone (plan steps model.5 .. model.22,
+ * cpu.rs:508-518 / cuda.rs:1590-1606): local [batch][128][h][w] and global
+ * [batch][384][h][w] in, the same shapes out, host buffers. */
+int lama_resblocks(lama_engine* e, const float* local_in, const float* global_in, int batch, int h, int w,
+                   int nblocks, float* local_out, float* global_out);
+
+/* Device-pointer variant of lama_resblocks. */
+int lama_resblocks_device(lama_engine* e, const float* d_local_in, const float* d_global_in, int batch, int h,
+                          int w, int nblocks, float* d_local_out, float* d_global_out);
+
+/* Message of the last failure on this engine ("" if none). */
+const char* lama_last_error(const lama_engine* e);
+
+/* Wait for all work queued on the engine's stream; reports device errors. */
+int lama_synchronize(lama_engine* e);
+
+/* The engine's cudaStream_t, for ordering caller work with the engine's. */
+void* lama_stream(lama_engine* e);
+
+/* Kernel launches one forward pass issues at this shape (after the plan for
+ * the shape exists; builds it if needed).  Returns < 0 on error. */
+int lama_launch_count(lama_engine* e, int batch, int h, int w);
+
+/* Per-kernel-class timing of one forward pass on device buffers: each launch
+ * is bracketed by CUDA events on the engine's stream.  Fills up to
+ * `max_stats` records; *n_stats is the number of classes. */
+typedef struct {
+  char name[32];
+  int launches;
+  double ms;       /* summed device time */
+  double flops;    /* algorithmic FLOPs (2 x MACs over real taps) */
+  double bytes;    /* algorithmic HBM bytes (operands + results, once) */
+} lama_kernel_stat;
+
+int lama_profile_forward(lama_engine* e, const float* d_in, int batch, int h, int w, float* d_out,
+                         lama_kernel_stat* stats, int max_stats, int* n_stats);
+
+/* Diagnostics (used by the layer-by-layer parity tests).
+ * lama_debug_run: run only the first `n_ops` launches of the f32 forward plan
+ * for this shape, eagerly, on host input [batch][4][h][w].
+ * lama_debug_read: copy launch `op`'s output tensor to `out` as fp32 (split
+ * pairs are summed); dims receives (batch, rows, cols, channels) of the
+ * stored NHWC layout including any halo, or (batch, C, H, W) for NCHW
+ * outputs; name receives the launch name (32 bytes).  With out == NULL only
+ * dims and name are filled.  Returns the launch count through the plan. */
+int lama_debug_run(lama_engine* e, const float* in, int batch, int h, int w, int n_ops);
+int lama_debug_read(lama_engine* e, int batch, int h, int w, int op, float* out, long long cap, int* dims,
+                    char* name);
+
+/* Free every device buffer and the engine. */
+void lama_close(lama_engine* e);
+
+/* ABI version of this header. */
+int lama_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LAMA_B200_H */

@@ -1,0 +1,362 @@
+// Implicit-GEMM convolution on the sm_100a tensor core (tcgen05 + TMEM + TMA).
+//
+// Replaces the reference's im2col + FP32 SIMT SGEMM pair (lama-rs/cuda/lama.cu
+// k_im2col :20-48 and k_sgemm_slab :363-456, launched from
+// lama-rs/src/cuda.rs:973-1139) and every elementwise pass that follows a
+// convolution there (k_bias_plane, k_bn_relu, k_bn_relu_add, lg_add_inplace,
+// lg_sigmoid, k_reflect_pad, k_convt_put, lg_copy for Concat): those become
+// the epilogue and the output addressing of this one kernel.
+//
+// Arithmetic: the reference is FP32.  Operands are carried as split bf16
+// pairs (x = hi + lo) and each K step issues three BF16 MMAs into one FP32
+// TMEM accumulator - hi*hi + hi*lo + lo*hi - which reproduces an FP32 dot
+// product to ~2^-16 relative (the dropped lo*lo term and the 16-bit operand
+// rounding) at the BF16 tensor-core rate.
+//
+// Structure: persistent CTAs (one per SM), 256 threads:
+//   warp 0      TMA producer (one elected thread), STAGES-deep smem ring
+//   warp 1      MMA issuer (one thread): 4 K-steps x 3 MMAs per 64-wide K block
+//   warp 2      TMEM allocator
+//   warps 4..7  epilogue: tcgen05.ld 32 columns at a time, fused BN/bias,
+//               ReLU, residual, sigmoid, split-bf16 or fp32 store, reflect halo
+// TMEM holds two BN-column accumulators so the epilogue of one tile overlaps
+// the main loop of the next.
+#include <cstdio>
+
+#include "gemm.cuh"
+#include "ptx.cuh"
+
+namespace lama {
+
+namespace {
+
+constexpr uint32_t A_PART = 128 * 64 * 2;  // one 128 x 64 bf16 operand tile
+
+__host__ __device__ constexpr int stages_for(int bn) {
+  // (2 * A_PART + 2 * bn * 128) bytes per stage, within ~200 KB
+  return bn <= 16 ? 5 : bn <= 64 ? 4 : bn <= 128 ? 3 : 2;
+}
+__host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 2 * A_PART + 2u * (uint32_t)bn * 128u; }
+__host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
+  return 2 * bn <= 32 ? 32 : 2 * bn <= 64 ? 64 : 2 * bn <= 128 ? 128 : 2 * bn <= 256 ? 256 : 512;
+}
+
+struct TileInfo {
+  int cls, nt, b, i0, j0;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
+  TileInfo ti;
+  int c = 0;
+  while (c + 1 < p.nclass && t >= p.cls[c + 1].tile0) c++;
+  const GemmClass& C = p.cls[c];
+  int lt = t - C.tile0;
+  ti.cls = c;
+  ti.nt = lt % C.ntiles_n;
+  int mt = lt / C.ntiles_n;
+  int per_img = p.tiles_y * p.tiles_x;
+  ti.b = mt / per_img;
+  int r = mt - ti.b * per_img;
+  ti.i0 = (r / p.tiles_x) * p.bh;
+  ti.j0 = (r % p.tiles_x) * p.bw;
+  return ti;
+}
+
+__device__ __forceinline__ int reflect_idx(int i, int n) {
+  if (n == 1) return 0;
+  int period = 2 * (n - 1);
+  int m = i % period;
+  if (m < 0) m += period;
+  return m >= n ? period - m : m;
+}
+
+// Padded positions whose value is interior coordinate q: q itself plus any
+// halo cells that reflect onto it.  Returns the count (<= 1 + 2*halo).
+__device__ __forceinline__ int halo_targets(int q, int n, int halo, int reflect, int* out) {
+  int cnt = 0;
+  out[cnt++] = q + halo;
+  if (reflect && halo > 0) {
+    for (int p = 0; p < halo; p++)
+      if (reflect_idx(p - halo, n) == q) out[cnt++] = p;
+    for (int p = n + halo; p < n + 2 * halo; p++)
+      if (reflect_idx(p - halo, n) == q) out[cnt++] = p;
+  }
+  return cnt;
+}
+
+template <int CH>
+__device__ __forceinline__ void store_split(const GemmParams& p, int b, int oy, int ox, int n, const float* v) {
+  int ty[7], tx[7];
+  int ny = halo_targets(oy, p.out_h, p.out_halo, p.out_reflect, ty);
+  int nx = halo_targets(ox, p.out_w, p.out_halo, p.out_reflect, tx);
+  uint32_t hi[CH / 2], lo[CH / 2];
+#pragma unroll
+  for (int k = 0; k < CH / 2; k++) split_pair(v[2 * k], v[2 * k + 1], hi[k], lo[k]);
+  const int hp = p.out_h + 2 * p.out_halo, wp = p.out_w + 2 * p.out_halo;
+  __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(p.out);
+  for (int a = 0; a < ny; a++)
+    for (int c = 0; c < nx; c++) {
+      long long off = (((long long)b * hp + ty[a]) * wp + tx[c]) * p.out_c + n;
+      uint4* dh = reinterpret_cast<uint4*>(base + off);
+      uint4* dl = reinterpret_cast<uint4*>(base + p.out_part + off);
+#pragma unroll
+      for (int k = 0; k < CH / 8; k++) {
+        dh[k] = make_uint4(hi[4 * k], hi[4 * k + 1], hi[4 * k + 2], hi[4 * k + 3]);
+        dl[k] = make_uint4(lo[4 * k], lo[4 * k + 1], lo[4 * k + 2], lo[4 * k + 3]);
+      }
+    }
+}
+
+template <int CH>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const GemmClass& C, int b, int oy, int ox,
+                                               int nloc, float* v) {
+  const int n = C.n0 + nloc;
+#pragma unroll
+  for (int k = 0; k < CH; k++) {
+    int nn = n + k;
+    float s = 1.f, t = 0.f;
+    if (nloc + k < C.nvalid) {
+      s = __ldg(p.scale + nn);
+      t = __ldg(p.shift + nn);
+    }
+    float x = v[k] * s;
+    x = x + t;
+    if (p.relu) x = x > 0.f ? x : 0.f;
+    v[k] = x;
+  }
+  if (p.skip) {
+    const int hp = p.out_h + 2 * p.out_halo, wp = p.out_w + 2 * p.out_halo;
+    long long off = (((long long)b * hp + oy + p.out_halo) * wp + ox + p.out_halo) * p.out_c + n;
+    const __nv_bfloat16* sb = reinterpret_cast<const __nv_bfloat16*>(p.skip);
+    const uint4* sh = reinterpret_cast<const uint4*>(sb + off);
+    const uint4* sl = reinterpret_cast<const uint4*>(sb + p.out_part + off);
+#pragma unroll
+    for (int k = 0; k < CH / 8; k++) {
+      uint4 h = sh[k], l = sl[k];
+      float2 f0 = join_pair(h.x, l.x), f1 = join_pair(h.y, l.y), f2 = join_pair(h.z, l.z), f3 = join_pair(h.w, l.w);
+      v[8 * k + 0] += f0.x; v[8 * k + 1] += f0.y;
+      v[8 * k + 2] += f1.x; v[8 * k + 3] += f1.y;
+      v[8 * k + 4] += f2.x; v[8 * k + 5] += f2.y;
+      v[8 * k + 6] += f3.x; v[8 * k + 7] += f3.y;
+    }
+  }
+  if (p.sigmoid) {
+#pragma unroll
+    for (int k = 0; k < CH; k++) {
+      float e = expf(-v[k]);
+      v[k] = 1.0f / (1.0f + e);
+    }
+  }
+  if (p.out_kind == OUT_SPLIT) {
+    store_split<CH>(p, b, oy, ox, n, v);
+  } else if (p.out_kind == OUT_F32_NHWC) {
+    const int hp = p.out_h + 2 * p.out_halo, wp = p.out_w + 2 * p.out_halo;
+    long long off = (((long long)b * hp + oy + p.out_halo) * wp + ox + p.out_halo) * p.out_c + n;
+    float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off);
+#pragma unroll
+    for (int k = 0; k < CH / 4; k++) d[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  } else {
+    float* o = reinterpret_cast<float*>(p.out);
+#pragma unroll
+    for (int k = 0; k < CH; k++)
+      if (nloc + k < C.nvalid)
+        o[(((long long)b * p.out_c + n + k) * p.out_h + oy) * p.out_w + ox] = v[k];
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ GemmParams p) {
+  constexpr int STAGES = stages_for(BN);
+  constexpr uint32_t B_PART = (uint32_t)BN * 128u;
+  constexpr uint32_t STAGE = stage_bytes(BN);
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  constexpr int CH = BN < 32 ? BN : 32;
+  constexpr uint32_t IDESC = idesc_bf16_f32(BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  const uint32_t smem0 = smem_u32(smem);
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+  auto tfull_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < p.nclass; i++) tma_prefetch(&p.bmap[i]);
+    for (int i = 0; i < GEMM_MAX_AMAPS; i++) tma_prefetch(&p.amap[i]);
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      const int subs_per_kb = 64 / p.cb;
+      const uint32_t sub_bytes = (uint32_t)p.cb * 128u * 2u;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile(p, t);
+        const GemmClass& C = p.cls[ti.cls];
+        int seg = 0;
+        for (int kb = 0; kb < C.nkb; kb++) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(full_bar(stage), STAGE);
+          const uint32_t sa = smem0 + (uint32_t)stage * STAGE;
+          for (int u = 0; u < subs_per_kb; u++) {
+            const int sub = kb * subs_per_kb + u;
+            while (seg + 1 < C.nseg && sub >= C.seg[seg + 1].sub0) seg++;
+            const GemmSeg& S = C.seg[seg];
+            const int r = sub - S.sub0;
+            const int tap = r / S.nblk, blk = r - tap * S.nblk;
+            const int cx = S.c0 + blk * p.cb;
+            const int x = ti.j0 * S.stride + S.dx[tap];
+            const int y = ti.i0 * S.stride + S.dy[tap];
+            tma_load_5d(sa + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, full_bar(stage));
+            tma_load_5d(sa + A_PART + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 1, full_bar(stage));
+          }
+          tma_load_3d(sa + 2 * A_PART, &p.bmap[ti.cls], kb * 64, ti.nt * BN, 0, full_bar(stage));
+          tma_load_3d(sa + 2 * A_PART + B_PART, &p.bmap[ti.cls], kb * 64, ti.nt * BN, 1, full_bar(stage));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const bool sw64 = (p.cb == 32);
+      const uint32_t a_sbo = sw64 ? 512u : 1024u;
+      const uint32_t a_layout = sw64 ? 4u : 2u;
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, it++) {
+        const TileInfo ti = decode_tile(p, t);
+        const GemmClass& C = p.cls[ti.cls];
+        const int acc = it & 1;
+        if (!mbar_wait(tempty_bar(acc), ((it >> 1) & 1) ^ 1, p.err, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < C.nkb; kb++) {
+          if (!mbar_wait(full_bar(stage), phase, p.err, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem0 + (uint32_t)stage * STAGE;
+          const uint32_t sb = sa + 2 * A_PART;
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const uint32_t aoff = sw64 ? (uint32_t)((k >> 1) * 8192 + (k & 1) * 32) : (uint32_t)(k * 32);
+            const uint64_t a_hi = smem_desc(sa + aoff, a_sbo, a_layout);
+            const uint64_t a_lo = smem_desc(sa + A_PART + aoff, a_sbo, a_layout);
+            const uint64_t b_hi = smem_desc(sb + k * 32, 1024u, 2u);
+            const uint64_t b_lo = smem_desc(sb + B_PART + k * 32, 1024u, 2u);
+            mma_bf16(d_tmem, a_lo, b_hi, IDESC, (kb | k) != 0 ? 1u : 0u);
+            mma_bf16(d_tmem, a_hi, b_lo, IDESC, 1u);
+            mma_bf16(d_tmem, a_hi, b_hi, IDESC, 1u);
+          }
+          mma_commit(empty_bar(stage));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (ok) mma_commit(tfull_bar(acc));
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------- epilogue
+    const int ew = warp - 4;
+    const int m = ew * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, it++) {
+      const TileInfo ti = decode_tile(p, t);
+      const GemmClass& C = p.cls[ti.cls];
+      const int acc = it & 1;
+      if (!mbar_wait(tfull_bar(acc), (it >> 1) & 1, p.err, 4)) break;
+      tc_fence_after();
+      const int i = ti.i0 + m / p.bw, j = ti.j0 + m % p.bw;
+      const bool valid = (i < p.mh) && (j < p.mw);
+      const int oy = i * C.oy_mul + C.oy_add, ox = j * C.ox_mul + C.ox_add;
+      const uint32_t trow = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int ch = 0; ch < BN / CH; ch++) {
+        float v[CH];
+        if constexpr (CH == 32) tmem_ld32(trow + ch * CH, v);
+        else tmem_ld16(trow + ch * CH, v);
+        tmem_wait_ld();
+        const int nloc = ti.nt * BN + ch * CH;
+        if (valid && nloc < C.nvalid) epilogue_chunk<CH>(p, C, ti.b, oy, ox, nloc, v);
+      }
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));
+    }
+  }
+
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int BN>
+int prepare_bn() {
+  const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256;
+  return (int)cudaFuncSetAttribute(k_conv_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+template <int BN>
+int launch_bn(const GemmParams& p, int grid, cudaStream_t stream) {
+  const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256;
+  k_conv_gemm<BN><<<grid, 256, smem, stream>>>(p);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+size_t conv_gemm_smem_bytes(int bn) { return (size_t)stages_for(bn) * stage_bytes(bn) + 1024 + 256; }
+int conv_gemm_stages(int bn) { return stages_for(bn); }
+
+// Opt every tile width into its dynamic shared memory size on the current
+// device; call once per device before the first launch.
+int conv_gemm_prepare() {
+  int e = 0;
+  if ((e = prepare_bn<16>())) return e;
+  if ((e = prepare_bn<64>())) return e;
+  if ((e = prepare_bn<128>())) return e;
+  if ((e = prepare_bn<192>())) return e;
+  return prepare_bn<256>();
+}
+
+int launch_conv_gemm(const GemmParams& p, int bn, int grid, cudaStream_t stream) {
+  switch (bn) {
+    case 16: return launch_bn<16>(p, grid, stream);
+    case 64: return launch_bn<64>(p, grid, stream);
+    case 128: return launch_bn<128>(p, grid, stream);
+    case 192: return launch_bn<192>(p, grid, stream);
+    case 256: return launch_bn<256>(p, grid, stream);
+    default: return -1;
+  }
+}
+
+}  // namespace lama

@@ -1,0 +1,1123 @@
+// The B200 big-lama engine: weights, per-shape plans, CUDA graphs, C ABI.
+//
+// Host side of the drop-in boundary declared in include/lama_b200.h.  It
+// replaces the reference's CUDA host engine (lama-rs/src/cuda.rs): module
+// bring-up (:225-275), the size-bucketed allocator (:91-184), the weight arena
+// and BN-fold staging (:330-387, :595-830), the device step tree (:903-962)
+// and the launch loop (:1542-1691).  Design differences, B200-first:
+//   * weights are repacked once at open into the operand layout of the
+//     tensor-core kernel: per launch and per tile class a [2][N][K] split-bf16
+//     matrix, with K-concatenated l2l|g2l and l2g|conv2 and the four
+//     ConvTranspose phase matrices (cuda.rs:566-577 tap table);
+//   * BatchNorm (cpu.rs:45-64) and conv biases fold into a per-channel
+//     scale/shift applied in the GEMM epilogue;
+//   * every activation buffer of a (batch, h, w) shape is allocated once (a
+//     "plan"); the whole pass is captured into one CUDA graph and replayed;
+//   * activations are NHWC split-bf16 with reflect halos written by the
+//     producing epilogue, so ReflectPad, Concat and the residual adds cost no
+//     launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "fft.cuh"
+#include "gemm.cuh"
+#include "lama_b200.h"
+#include "pointwise.cuh"
+#include "weights.h"
+
+using namespace lama;
+
+namespace {
+
+// ------------------------------------------------------------------ errors
+struct EngineError {
+  int code;
+  std::string msg;
+};
+
+#define CK(x)                                                                                   \
+  do {                                                                                          \
+    cudaError_t e_ = (x);                                                                       \
+    if (e_ != cudaSuccess) throw EngineError{LAMA_ECUDA, std::string(#x) + ": " + cudaGetErrorString(e_)}; \
+  } while (0)
+
+#define CKL(x)                                                                                  \
+  do {                                                                                          \
+    int e_ = (x);                                                                               \
+    if (e_ != 0)                                                                                \
+      throw EngineError{LAMA_ECUDA, std::string(#x) + ": " + cudaGetErrorString((cudaError_t)e_)}; \
+  } while (0)
+
+// ------------------------------------------------------------------ host bf16
+uint16_t f2bf(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+float bf2f(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+// ------------------------------------------------------------------ device memory
+struct DevMem {
+  std::vector<void*> ptrs;
+  size_t total = 0;
+  void* alloc(size_t bytes, bool zero = true) {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, std::max<size_t>(bytes, 256));
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      throw EngineError{LAMA_ENOMEM, "cudaMalloc(" + std::to_string(bytes) + " bytes): " + cudaGetErrorString(e)};
+    }
+    if (zero) CK(cudaMemset(p, 0, std::max<size_t>(bytes, 256)));
+    ptrs.push_back(p);
+    total += bytes;
+    return p;
+  }
+  void free_all() {
+    for (void* p : ptrs) cudaFree(p);
+    ptrs.clear();
+    total = 0;
+  }
+  ~DevMem() { free_all(); }
+};
+
+// ------------------------------------------------------------------ tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !p)
+      throw EngineError{LAMA_ECUDA, "cuTensorMapEncodeTiled is not available from the driver"};
+    fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  }
+  return fn;
+}
+
+// A split-bf16 NHWC activation: [2][B][H+2halo][W+2halo][C].
+struct Act {
+  void* p = nullptr;
+  int B = 0, H = 0, W = 0, C = 0, halo = 0;
+  long long part() const { return (long long)B * (H + 2 * halo) * (W + 2 * halo) * C; }
+  size_t bytes() const { return (size_t)part() * 2 * 2; }
+};
+
+CUtensorMap act_map(const Act& a, int cb, int bw, int bh, int stride, bool interior) {
+  CUtensorMap m;
+  const int hp = a.H + 2 * a.halo, wp = a.W + 2 * a.halo;
+  char* base = (char*)a.p;
+  cuuint64_t dims[5];
+  if (interior) {
+    base += (((size_t)a.halo * wp + a.halo) * a.C) * 2;
+    dims[1] = (cuuint64_t)a.W;
+    dims[2] = (cuuint64_t)a.H;
+  } else {
+    dims[1] = (cuuint64_t)wp;
+    dims[2] = (cuuint64_t)hp;
+  }
+  dims[0] = (cuuint64_t)a.C;
+  dims[3] = (cuuint64_t)a.B;
+  dims[4] = 2;
+  cuuint64_t strides[4] = {(cuuint64_t)a.C * 2, (cuuint64_t)wp * a.C * 2, (cuuint64_t)hp * wp * a.C * 2,
+                           (cuuint64_t)a.part() * 2};
+  cuuint32_t box[5] = {(cuuint32_t)cb, (cuuint32_t)(bw * stride), (cuuint32_t)(bh * stride), 1, 1};
+  cuuint32_t estr[5] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, base, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           cb == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw EngineError{LAMA_ECUDA, "cuTensorMapEncodeTiled (activation) failed: " + std::to_string((int)r)};
+  return m;
+}
+
+// ------------------------------------------------------------------ weights
+struct WClass {
+  int n = 0, npad = 0, k = 0;
+  void* w = nullptr;  // [2][npad][k] bf16
+};
+
+struct GemmW {
+  std::vector<WClass> cls;
+  float* scale = nullptr;
+  float* shift = nullptr;
+  int nout = 0;
+};
+
+CUtensorMap w_map(const WClass& c, int bn) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)c.k, (cuuint64_t)c.npad, 2};
+  cuuint64_t strides[2] = {(cuuint64_t)c.k * 2, (cuuint64_t)c.npad * c.k * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)bn, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c.w, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw EngineError{LAMA_ECUDA, "cuTensorMapEncodeTiled (weights) failed: " + std::to_string((int)r)};
+  return m;
+}
+
+struct FfcW {
+  GemmW conv1, fu, out;
+};
+
+struct Weights {
+  GemmW m1, m2, m3, m4;
+  std::vector<FfcW> ffc;  // 36: block 0 conv1, block 0 conv2, ...
+  GemmW ct[3];
+  GemmW outc;
+};
+
+struct Loader {
+  const WeightFile& wf;
+  DevMem& mem;
+  std::vector<float> get(const std::string& name, const std::vector<int64_t>& shape) {
+    std::vector<float> v;
+    std::string err;
+    if (!wf.f32(name, shape, v, err)) throw EngineError{LAMA_EWEIGHTS, err};
+    return v;
+  }
+  // cpu.rs:45-64 (`Bn::load`): s = w / sqrt(var + 1e-5), t = b - mean * s, in f32.
+  void bn(const std::string& p, int c, std::vector<float>& s, std::vector<float>& t) {
+    auto w = get(p + ".weight", {c}), b = get(p + ".bias", {c});
+    auto mean = get(p + ".running_mean", {c}), var = get(p + ".running_var", {c});
+    for (int i = 0; i < c; i++) {
+      float sd = std::sqrt(var[i] + 1e-5f);
+      float sc = w[i] / sd;
+      float ms = mean[i] * sc;
+      s.push_back(sc);
+      t.push_back(b[i] - ms);
+    }
+  }
+  // One class: fp32 [n][k] -> split bf16 [2][npad][k] on the device.
+  WClass upload(const std::vector<float>& m, int n, int k) {
+    WClass c;
+    c.n = n;
+    c.k = k;
+    c.npad = (n + 15) / 16 * 16;
+    std::vector<uint16_t> h((size_t)2 * c.npad * k, 0);
+    for (int i = 0; i < n; i++)
+      for (int j = 0; j < k; j++) {
+        float v = m[(size_t)i * k + j];
+        uint16_t hi = f2bf(v);
+        uint16_t lo = f2bf(v - bf2f(hi));
+        h[(size_t)i * k + j] = hi;
+        h[(size_t)c.npad * k + (size_t)i * k + j] = lo;
+      }
+    c.w = mem.alloc(h.size() * 2, false);
+    CK(cudaMemcpy(c.w, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+    return c;
+  }
+  void affine(GemmW& g, const std::vector<float>& s, const std::vector<float>& t) {
+    g.nout = (int)s.size();
+    g.scale = (float*)mem.alloc(s.size() * 4, false);
+    g.shift = (float*)mem.alloc(t.size() * 4, false);
+    CK(cudaMemcpy(g.scale, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(g.shift, t.data(), t.size() * 4, cudaMemcpyHostToDevice));
+  }
+};
+
+// K order of a kxk conv segment: tap-major (ky, kx), then input channel.
+void put_conv(std::vector<float>& m, int ktot, int kofs, const std::vector<float>& w, int cout, int cin, int kk,
+              int row0 = 0) {
+  for (int n = 0; n < cout; n++)
+    for (int t = 0; t < kk * kk; t++)
+      for (int c = 0; c < cin; c++)
+        m[(size_t)(row0 + n) * ktot + kofs + t * cin + c] = w[((size_t)n * cin + c) * kk * kk + t];
+}
+
+void load_weights(const WeightFile& wf, DevMem& mem, Weights& W) {
+  Loader L{wf, mem};
+  std::vector<float> s, t;
+  // model.1: 7x7 4->64 valid.  K = 8 row taps x 32, channel = kx*4 + c (28 used).
+  {
+    auto w = L.get("model.1.ffc.convl2l.weight", {64, 4, 7, 7});
+    std::vector<float> m((size_t)64 * 256, 0.f);
+    for (int n = 0; n < 64; n++)
+      for (int ky = 0; ky < 7; ky++)
+        for (int kx = 0; kx < 7; kx++)
+          for (int c = 0; c < 4; c++) m[(size_t)n * 256 + ky * 32 + kx * 4 + c] = w[((n * 4 + c) * 7 + ky) * 7 + kx];
+    W.m1.cls.push_back(L.upload(m, 64, 256));
+    s.clear(); t.clear();
+    L.bn("model.1.bn_l", 64, s, t);
+    L.affine(W.m1, s, t);
+  }
+  // model.2, model.3: 3x3 stride-2 reflect
+  const int enc[2][3] = {{2, 64, 128}, {3, 128, 256}};
+  GemmW* encw[2] = {&W.m2, &W.m3};
+  for (int e = 0; e < 2; e++) {
+    const int idx = enc[e][0], cin = enc[e][1], cout = enc[e][2];
+    auto w = L.get("model." + std::to_string(idx) + ".ffc.convl2l.weight", {cout, cin, 3, 3});
+    std::vector<float> m((size_t)cout * 9 * cin, 0.f);
+    put_conv(m, 9 * cin, 0, w, cout, cin, 3);
+    encw[e]->cls.push_back(L.upload(m, cout, 9 * cin));
+    s.clear(); t.clear();
+    L.bn("model." + std::to_string(idx) + ".bn_l", cout, s, t);
+    L.affine(*encw[e], s, t);
+  }
+  // model.4: 256 -> 128 local (l2l) + 384 global (l2g)
+  {
+    auto l2l = L.get("model.4.ffc.convl2l.weight", {128, 256, 3, 3});
+    auto l2g = L.get("model.4.ffc.convl2g.weight", {384, 256, 3, 3});
+    std::vector<float> m((size_t)512 * 2304, 0.f);
+    put_conv(m, 2304, 0, l2l, 128, 256, 3, 0);
+    put_conv(m, 2304, 0, l2g, 384, 256, 3, 128);
+    W.m4.cls.push_back(L.upload(m, 512, 2304));
+    s.clear(); t.clear();
+    L.bn("model.4.bn_l", 128, s, t);
+    L.bn("model.4.bn_g", 384, s, t);
+    L.affine(W.m4, s, t);
+  }
+  // 18 resblocks x 2 FFC layers
+  for (int blk = 5; blk <= 22; blk++)
+    for (int sub = 1; sub <= 2; sub++) {
+      const std::string part = "model." + std::to_string(blk) + ".conv" + std::to_string(sub);
+      const std::string p = part + ".ffc";
+      FfcW f;
+      auto c1 = L.get(p + ".convg2g.conv1.0.weight", {192, 384, 1, 1});
+      f.conv1.cls.push_back(L.upload(c1, 192, 384));
+      s.clear(); t.clear();
+      L.bn(p + ".convg2g.conv1.1", 192, s, t);
+      L.affine(f.conv1, s, t);
+      auto fu = L.get(p + ".convg2g.fu.conv_layer.weight", {384, 384, 1, 1});
+      f.fu.cls.push_back(L.upload(fu, 384, 384));
+      s.clear(); t.clear();
+      L.bn(p + ".convg2g.fu.bn", 384, s, t);
+      L.affine(f.fu, s, t);
+      // local class: 3x3 over all 512 channels = [l2l | g2l]
+      auto l2l = L.get(p + ".convl2l.weight", {128, 128, 3, 3});
+      auto g2l = L.get(p + ".convg2l.weight", {128, 384, 3, 3});
+      std::vector<float> ml((size_t)128 * 4608, 0.f);
+      for (int n = 0; n < 128; n++)
+        for (int tp = 0; tp < 9; tp++) {
+          for (int c = 0; c < 128; c++) ml[(size_t)n * 4608 + tp * 512 + c] = l2l[((size_t)n * 128 + c) * 9 + tp];
+          for (int c = 0; c < 384; c++)
+            ml[(size_t)n * 4608 + tp * 512 + 128 + c] = g2l[((size_t)n * 384 + c) * 9 + tp];
+        }
+      f.out.cls.push_back(L.upload(ml, 128, 4608));
+      // global class: 3x3 over the 128 local channels (l2g), then 1x1 over S (conv2)
+      auto l2g = L.get(p + ".convl2g.weight", {384, 128, 3, 3});
+      auto cv2 = L.get(p + ".convg2g.conv2.weight", {384, 192, 1, 1});
+      std::vector<float> mg((size_t)384 * 1344, 0.f);
+      put_conv(mg, 1344, 0, l2g, 384, 128, 3);
+      for (int n = 0; n < 384; n++)
+        for (int c = 0; c < 192; c++) mg[(size_t)n * 1344 + 1152 + c] = cv2[(size_t)n * 192 + c];
+      f.out.cls.push_back(L.upload(mg, 384, 1344));
+      s.clear(); t.clear();
+      L.bn(part + ".bn_l", 128, s, t);
+      L.bn(part + ".bn_g", 384, s, t);
+      L.affine(f.out, s, t);
+      W.ffc.push_back(std::move(f));
+    }
+  // ConvTranspose2d k3 s2 p1 op1 as four output phases; weight [cin][cout][3][3].
+  // Phase (py, px) taps: (ky, kx, dy, dx) with input pixel (i + dy, j + dx).
+  static const int taps[4][4][4] = {
+      {{1, 1, 0, 0}},
+      {{1, 0, 0, 1}, {1, 2, 0, 0}},
+      {{0, 1, 1, 0}, {2, 1, 0, 0}},
+      {{0, 0, 1, 1}, {0, 2, 1, 0}, {2, 0, 0, 1}, {2, 2, 0, 0}}};
+  static const int ntaps[4] = {1, 2, 2, 4};
+  const int ups[3][4] = {{24, 25, 512, 256}, {27, 28, 256, 128}, {30, 31, 128, 64}};
+  for (int u = 0; u < 3; u++) {
+    const int idx = ups[u][0], bnx = ups[u][1], cin = ups[u][2], cout = ups[u][3];
+    auto w = L.get("model." + std::to_string(idx) + ".weight", {cin, cout, 3, 3});
+    auto bias = L.get("model." + std::to_string(idx) + ".bias", {cout});
+    for (int ph = 0; ph < 4; ph++) {
+      const int k = ntaps[ph] * cin;
+      std::vector<float> m((size_t)cout * k, 0.f);
+      for (int n = 0; n < cout; n++)
+        for (int ti = 0; ti < ntaps[ph]; ti++) {
+          const int ky = taps[ph][ti][0], kx = taps[ph][ti][1];
+          for (int c = 0; c < cin; c++) m[(size_t)n * k + ti * cin + c] = w[(((size_t)c * cout + n) * 3 + ky) * 3 + kx];
+        }
+      W.ct[u].cls.push_back(L.upload(m, cout, k));
+    }
+    s.clear(); t.clear();
+    L.bn("model." + std::to_string(bnx), cout, s, t);
+    // (acc + bias) * s + t  ->  acc * s + (bias * s + t)
+    for (int n = 0; n < cout; n++) t[n] = bias[n] * s[n] + t[n];
+    L.affine(W.ct[u], s, t);
+  }
+  // OutConv 7x7 64 -> 3 with bias, over the reflect-padded input
+  {
+    auto w = L.get("model.34.weight", {3, 64, 7, 7});
+    auto bias = L.get("model.34.bias", {3});
+    std::vector<float> m((size_t)3 * 49 * 64, 0.f);
+    put_conv(m, 49 * 64, 0, w, 3, 64, 7);
+    W.outc.cls.push_back(L.upload(m, 3, 49 * 64));
+    std::vector<float> one(16, 1.f), sh(16, 0.f);
+    for (int n = 0; n < 3; n++) sh[n] = bias[n];
+    L.affine(W.outc, one, sh);
+  }
+}
+
+// ------------------------------------------------------------------ ops
+enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
+
+struct Op {
+  OpKind kind;
+  std::string name;
+  int bn = 0, grid = 0;
+  std::unique_ptr<GemmParams> g;
+  FftParams f{};
+  UnfoldParams u{};
+  CompositeParams c{};
+  ConvertParams cv{};
+  double flops = 0, bytes = 0;
+  // output tensor, for the diagnostics entry points: split bf16 or fp32,
+  // dims = (B, rows, cols, channels) of the stored layout (halo included;
+  // NCHW outputs report (B, C, H, W)).
+  void* out_ptr = nullptr;
+  int out_split = 0;
+  long long out_part = 0;
+  int dims[4] = {0, 0, 0, 0};
+};
+
+int launch_op(const Op& op, cudaStream_t st) {
+  switch (op.kind) {
+    case OP_GEMM: return launch_conv_gemm(*op.g, op.bn, op.grid, st);
+    case OP_RFFT: return launch_rfft2(op.f, st);
+    case OP_IRFFT: return launch_irfft2(op.f, st);
+    case OP_UNFOLD_F32: return launch_unfold_f32(op.u, st);
+    case OP_UNFOLD_U8: return launch_unfold_u8(op.u, st);
+    case OP_COMPOSITE: return launch_composite(op.c, st);
+    case OP_TO_SPLIT: return launch_nchw_to_split(op.cv, st);
+    case OP_TO_NCHW: return launch_split_to_nchw(op.cv, st);
+  }
+  return -1;
+}
+
+struct SegSpec {
+  int amap, c0, nch, stride;
+  std::vector<std::pair<int, int>> taps;  // (dy, dx)
+};
+struct ClassSpec {
+  int wc, n0, nvalid;
+  int oy_mul = 1, oy_add = 0, ox_mul = 1, ox_add = 0;
+  std::vector<SegSpec> segs;
+};
+
+ClassSpec one_seg(int wc, int n0, int nvalid, SegSpec seg) {
+  ClassSpec c{wc, n0, nvalid};
+  c.segs.push_back(std::move(seg));
+  return c;
+}
+struct AmapSpec {
+  Act act;
+  int stride;
+  bool interior;
+};
+struct OutSpec {
+  int kind;
+  void* p;
+  long long part;
+  int c, h, w, halo, reflect;
+  const void* skip;
+};
+
+void choose_tile(int mh, int mw, int& bh, int& bw) {
+  long long best = -1;
+  for (int cand = 128; cand >= 8; cand >>= 1) {
+    const int ch = 128 / cand;
+    const long long cost = (long long)((mh + ch - 1) / ch) * ch * ((mw + cand - 1) / cand) * cand;
+    if (best < 0 || cost < best) {
+      best = cost;
+      bw = cand;
+      bh = ch;
+    }
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ engine
+struct Plan {
+  int kind = 0;  // 0 f32 forward, 1 u8 inpaint, 2 resblocks
+  int B = 0, H = 0, W = 0, h = 0, w = 0, nblocks = 0;
+  DevMem mem;
+  float* in_f32 = nullptr;
+  float* out = nullptr;
+  uint8_t *rgb = nullptr, *mask = nullptr, *out_rgb = nullptr;
+  float *l_in = nullptr, *g_in = nullptr, *l_out = nullptr, *g_out = nullptr;
+  std::vector<Op> ops;
+  cudaGraphExec_t exec = nullptr;
+  ~Plan() {
+    if (exec) cudaGraphExecDestroy(exec);
+  }
+};
+
+struct lama_engine {
+  int device = 0;
+  int sms = 148;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  DevMem wmem;
+  Weights W;
+  int* d_err = nullptr;
+  std::map<std::tuple<int, int, int, int, int, int, int>, std::unique_ptr<Plan>> plans;
+};
+
+namespace {
+
+struct Builder {
+  lama_engine& e;
+  Plan& pl;
+
+  Act act(int B, int H, int W, int C, int halo) {
+    Act a;
+    a.B = B; a.H = H; a.W = W; a.C = C; a.halo = halo;
+    a.p = pl.mem.alloc(a.bytes());
+    return a;
+  }
+
+  int choose_bn(const std::vector<int>& ns, int m_tiles) {
+    if (ns.size() == 1 && ns[0] < 16) return 16;
+    const int cands[4] = {256, 192, 128, 64};
+    int fallback = 0;
+    for (int bn : cands) {
+      bool ok = true;
+      long long tiles = 0;
+      for (int n : ns) {
+        if (n % bn) ok = false;
+        tiles += (long long)m_tiles * (n / std::max(bn, 1));
+      }
+      if (!ok) continue;
+      fallback = bn;
+      if (tiles >= e.sms) return bn;
+    }
+    return fallback;
+  }
+
+  void gemm(const std::string& name, const GemmW& Wt, const std::vector<AmapSpec>& amaps,
+            const std::vector<ClassSpec>& classes, int cb, int B, int mh, int mw, const OutSpec& o, int relu,
+            int sigmoid, double flops, int force_bn = 0) {
+    Op op;
+    op.kind = OP_GEMM;
+    op.name = name;
+    op.flops = flops;
+    op.g.reset(new GemmParams());
+    GemmParams& p = *op.g;
+    memset(&p, 0, sizeof(p));
+    int bh = 1, bw = 128;
+    choose_tile(mh, mw, bh, bw);
+    p.cb = cb;
+    p.batch = B;
+    p.mh = mh;
+    p.mw = mw;
+    p.bh = bh;
+    p.bw = bw;
+    p.tiles_y = (mh + bh - 1) / bh;
+    p.tiles_x = (mw + bw - 1) / bw;
+    p.m_tiles = B * p.tiles_y * p.tiles_x;
+    std::vector<int> ns;
+    for (auto& c : classes) ns.push_back(c.nvalid);
+    const int bn = force_bn ? force_bn : choose_bn(ns, p.m_tiles);
+    if (!bn) throw EngineError{LAMA_EUNSUPPORTED, name + ": no tile width divides the output channels"};
+    op.bn = bn;
+    for (size_t i = 0; i < amaps.size(); i++)
+      p.amap[i] = act_map(amaps[i].act, cb, bw, bh, amaps[i].stride, amaps[i].interior);
+    for (size_t i = amaps.size(); i < (size_t)GEMM_MAX_AMAPS; i++) p.amap[i] = p.amap[0];
+    p.nclass = (int)classes.size();
+    int tile0 = 0;
+    for (size_t ci = 0; ci < classes.size(); ci++) {
+      const ClassSpec& cs = classes[ci];
+      GemmClass& C = p.cls[ci];
+      const WClass& wc = Wt.cls[cs.wc];
+      p.bmap[ci] = w_map(wc, bn);
+      C.n0 = cs.n0;
+      C.nvalid = cs.nvalid;
+      C.ntiles_n = (cs.nvalid + bn - 1) / bn;
+      C.oy_mul = cs.oy_mul; C.oy_add = cs.oy_add; C.ox_mul = cs.ox_mul; C.ox_add = cs.ox_add;
+      C.nseg = (int)cs.segs.size();
+      int sub = 0;
+      for (size_t si = 0; si < cs.segs.size(); si++) {
+        const SegSpec& ss = cs.segs[si];
+        GemmSeg& S = C.seg[si];
+        S.amap = ss.amap;
+        S.c0 = ss.c0;
+        S.nblk = ss.nch / cb;
+        S.ntaps = (int)ss.taps.size();
+        S.stride = ss.stride;
+        S.sub0 = sub;
+        for (size_t t = 0; t < ss.taps.size(); t++) {
+          S.dy[t] = (int8_t)ss.taps[t].first;
+          S.dx[t] = (int8_t)ss.taps[t].second;
+        }
+        sub += S.nblk * S.ntaps;
+      }
+      if ((sub * cb) % 64) throw EngineError{LAMA_EUNSUPPORTED, name + ": K is not a multiple of 64"};
+      C.nkb = sub * cb / 64;
+      if (C.nkb * 64 != wc.k)
+        throw EngineError{LAMA_EUNSUPPORTED, name + ": K mismatch between plan and packed weights"};
+      C.tile0 = tile0;
+      tile0 += p.m_tiles * C.ntiles_n;
+    }
+    p.total_tiles = tile0;
+    p.scale = Wt.scale;
+    p.shift = Wt.shift;
+    p.relu = relu;
+    p.sigmoid = sigmoid;
+    p.out_kind = o.kind;
+    p.out = o.p;
+    p.out_part = o.part;
+    p.out_c = o.c;
+    p.out_h = o.h;
+    p.out_w = o.w;
+    p.out_halo = o.halo;
+    p.out_reflect = o.reflect;
+    p.skip = o.skip;
+    p.err = e.d_err;
+    op.grid = std::min(p.total_tiles, e.sms);
+    op.out_ptr = o.p;
+    op.out_split = o.kind == OUT_SPLIT;
+    op.out_part = o.part;
+    if (o.kind == OUT_F32_NCHW) {
+      op.dims[0] = B; op.dims[1] = o.c; op.dims[2] = o.h; op.dims[3] = o.w;
+    } else {
+      op.dims[0] = B; op.dims[1] = o.h + 2 * o.halo; op.dims[2] = o.w + 2 * o.halo; op.dims[3] = o.c;
+    }
+    pl.ops.push_back(std::move(op));
+  }
+
+  static OutSpec split_out(const Act& a, const void* skip = nullptr) {
+    return OutSpec{OUT_SPLIT, a.p, a.part(), a.C, a.H, a.W, a.halo, a.halo > 0 ? 1 : 0, skip};
+  }
+
+  static std::vector<std::pair<int, int>> square_taps(int k, int off) {
+    std::vector<std::pair<int, int>> t;
+    for (int ky = 0; ky < k; ky++)
+      for (int kx = 0; kx < k; kx++) t.push_back({ky + off, kx + off});
+    return t;
+  }
+
+  float2* twiddles(int n) {
+    std::vector<float2> t(n);
+    for (int k = 0; k < n; k++) {
+      double a = 2.0 * M_PI * (double)k / (double)n;
+      t[k] = make_float2((float)std::cos(a), (float)std::sin(a));
+    }
+    float2* d = (float2*)pl.mem.alloc((size_t)n * sizeof(float2), false);
+    CK(cudaMemcpy(d, t.data(), (size_t)n * sizeof(float2), cudaMemcpyHostToDevice));
+    return d;
+  }
+
+  static int log2_or_neg(int n) {
+    if (n <= 0 || (n & (n - 1))) return -1;
+    int l = 0;
+    while ((1 << l) < n) l++;
+    return l;
+  }
+
+  // Resblock stack on XA (in place), using XB / spectral scratch.
+  void resblocks(const Act& XA, const Act& XB, int nblocks) {
+    const int B = XA.B, h = XA.H, w = XA.W, wh = w / 2 + 1;
+    float* feat = (float*)pl.mem.alloc((size_t)B * h * w * 192 * 4);
+    Act spec{};
+    spec.B = B; spec.H = 1; spec.W = h * wh; spec.C = 384; spec.halo = 0;
+    spec.p = pl.mem.alloc(spec.bytes());
+    float* fu = (float*)pl.mem.alloc((size_t)B * h * wh * 384 * 4);
+    Act S = act(B, h, w, 192, 0);
+    FftParams fp{};
+    fp.batch = B; fp.c = 192; fp.h = h; fp.w = w; fp.wh = wh;
+    fp.log2h = log2_or_neg(h); fp.log2w = log2_or_neg(w);
+    fp.lmax = std::max(h, w);
+    fp.scale = (float)(1.0 / std::sqrt((double)h * (double)w));
+    fp.tw_h = twiddles(h);
+    fp.tw_w = twiddles(w);
+    fp.feat = feat;
+    fp.spec = spec.p;
+    fp.spec_part = spec.part();
+    fp.fu = fu;
+    fp.s_out = S.p;
+    fp.s_part = S.part();
+    const size_t budget = 200 * 1024;
+    const size_t fixed = sizeof(float2) * ((size_t)16 * fp.lmax + h + w);
+    const size_t per_ch = sizeof(float2) * (size_t)h * wh;
+    if (fixed + per_ch > budget)
+      throw EngineError{LAMA_EUNSUPPORTED, "latent plane " + std::to_string(h) + "x" + std::to_string(w) +
+                                               " is too large for the single-pass spectral kernels"};
+    fp.cg = (int)std::min<size_t>(8, (budget - fixed) / per_ch);
+    const double px = (double)B * h * w, pxs = (double)B * h * wh;
+    for (int blk = 0; blk < nblocks; blk++)
+      for (int sub = 0; sub < 2; sub++) {
+        const FfcW& F = e.W.ffc[(size_t)blk * 2 + sub];
+        const Act& Xin = sub == 0 ? XA : XB;
+        const Act& Xout = sub == 0 ? XB : XA;
+        const std::string tag = "b" + std::to_string(blk) + "." + std::to_string(sub + 1);
+        // conv1 1x1 384 -> 192 on the global channels, BN, ReLU -> feat (fp32)
+        gemm("spectral_conv1", F.conv1, {{Xin, 1, false}}, {one_seg(0, 0, 192, SegSpec{0, 128, 384, 1, {{1, 1}}})}, 64, B, h, w,
+             OutSpec{OUT_F32_NHWC, feat, 0, 192, h, w, 0, 0, nullptr}, 1, 0, 2.0 * px * 192 * 384);
+        Op r;
+        r.kind = OP_RFFT;
+        r.name = "rfft2";
+        r.f = fp;
+        r.bytes = px * 192 * 4 + pxs * 384 * 4;
+        r.out_ptr = spec.p; r.out_split = 1; r.out_part = spec.part();
+        r.dims[0] = B; r.dims[1] = h; r.dims[2] = wh; r.dims[3] = 384;
+        pl.ops.push_back(std::move(r));
+        // FourierUnit 1x1 384 -> 384 on the stacked spectrum, BN, ReLU -> fu (fp32)
+        gemm("fourier_conv", F.fu, {{spec, 1, false}}, {one_seg(0, 0, 384, SegSpec{0, 0, 384, 1, {{0, 0}}})}, 64, B, 1, h * wh,
+             OutSpec{OUT_F32_NHWC, fu, 0, 384, 1, h * wh, 0, 0, nullptr}, 1, 0, 2.0 * pxs * 384 * 384);
+        Op ir;
+        ir.kind = OP_IRFFT;
+        ir.name = "irfft2";
+        ir.f = fp;
+        ir.bytes = pxs * 384 * 4 + px * 192 * 4 + px * 192 * 4;
+        ir.out_ptr = S.p; ir.out_split = 1; ir.out_part = S.part();
+        ir.dims[0] = B; ir.dims[1] = h; ir.dims[2] = w; ir.dims[3] = 192;
+        pl.ops.push_back(std::move(ir));
+        // FFC outputs: local = 3x3 over [x_l | x_g]; global = 3x3 over x_l + 1x1 over S
+        ClassSpec cl{0, 0, 128};
+        cl.segs.push_back({0, 0, 512, 1, square_taps(3, 0)});
+        ClassSpec cgl{1, 128, 384};
+        cgl.segs.push_back({0, 0, 128, 1, square_taps(3, 0)});
+        cgl.segs.push_back({1, 0, 192, 1, {{0, 0}}});
+        gemm("ffc_out", F.out, {{Xin, 1, false}, {S, 1, false}}, {cl, cgl}, 64, B, h, w,
+             split_out(Xout, sub == 1 ? XA.p : nullptr), 1, 0, 2.0 * px * (128.0 * 4608 + 384.0 * 1344));
+      }
+  }
+
+  void core(const Act& U, int B, int H, int W, float* out) {
+    const int h2 = H / 2, w2 = W / 2, h4 = H / 4, w4 = W / 4, h8 = H / 8, w8 = W / 8;
+    Act X1 = act(B, H, W, 64, 1);
+    Act X2 = act(B, h2, w2, 128, 1);
+    Act X3 = act(B, h4, w4, 256, 1);
+    Act XA = act(B, h8, w8, 512, 1);
+    Act XB = act(B, h8, w8, 512, 1);
+    // model.1: 7x7 valid over the pad-3 input: 8 row taps (the 8th has zero weights)
+    {
+      ClassSpec c{0, 0, 64};
+      std::vector<std::pair<int, int>> t;
+      for (int ky = 0; ky < 8; ky++) t.push_back({ky, 0});
+      c.segs.push_back({0, 0, 32, 1, t});
+      gemm("model1_7x7", e.W.m1, {{U, 1, false}}, {c}, 32, B, H, W, split_out(X1), 1, 0,
+           2.0 * B * H * W * 64 * 196);
+    }
+    // model.2 .. model.4: 3x3 stride 2, reflect pad 1 (the halo)
+    {
+      ClassSpec c{0, 0, 128};
+      c.segs.push_back({0, 0, 64, 2, square_taps(3, 0)});
+      gemm("model2_3x3s2", e.W.m2, {{X1, 2, false}}, {c}, 64, B, h2, w2, split_out(X2), 1, 0,
+           2.0 * B * h2 * w2 * 128 * 576);
+    }
+    {
+      ClassSpec c{0, 0, 256};
+      c.segs.push_back({0, 0, 128, 2, square_taps(3, 0)});
+      gemm("model3_3x3s2", e.W.m3, {{X2, 2, false}}, {c}, 64, B, h4, w4, split_out(X3), 1, 0,
+           2.0 * B * h4 * w4 * 256 * 1152);
+    }
+    {
+      ClassSpec c{0, 0, 512};
+      c.segs.push_back({0, 0, 256, 2, square_taps(3, 0)});
+      gemm("model4_3x3s2", e.W.m4, {{X3, 2, false}}, {c}, 64, B, h8, w8, split_out(XA), 1, 0,
+           2.0 * B * h8 * w8 * 512 * 2304);
+    }
+    resblocks(XA, XB, 18);
+    // decoder: three ConvTranspose2d + BN + ReLU as phase GEMMs, Concat is XA itself
+    static const int taps[4][4][2] = {{{0, 0}}, {{0, 1}, {0, 0}}, {{1, 0}, {0, 0}}, {{1, 1}, {1, 0}, {0, 1}, {0, 0}}};
+    static const int ntaps[4] = {1, 2, 2, 4};
+    Act U1 = act(B, 2 * h8, 2 * w8, 256, 0);
+    Act U2 = act(B, 4 * h8, 4 * w8, 128, 0);
+    Act U3 = act(B, H, W, 64, 3);
+    const Act ins[3] = {XA, U1, U2};
+    const Act outs[3] = {U1, U2, U3};
+    const char* names[3] = {"convT1", "convT2", "convT3"};
+    for (int u = 0; u < 3; u++) {
+      const Act& in = ins[u];
+      const int cout = outs[u].C;
+      std::vector<ClassSpec> cls;
+      for (int ph = 0; ph < 4; ph++) {
+        ClassSpec c{ph, 0, cout, 2, ph / 2, 2, ph % 2};
+        std::vector<std::pair<int, int>> t;
+        for (int ti = 0; ti < ntaps[ph]; ti++) t.push_back({taps[ph][ti][0], taps[ph][ti][1]});
+        c.segs.push_back({0, 0, in.C, 1, t});
+        cls.push_back(c);
+      }
+      gemm(names[u], e.W.ct[u], {{in, 1, true}}, cls, 64, B, in.H, in.W, split_out(outs[u]), 1, 0,
+           2.0 * B * in.H * in.W * cout * in.C * 9);
+    }
+    // OutConv 7x7 64 -> 3 over the reflect-pad-3 halo, + bias, sigmoid -> fp32 NCHW
+    {
+      ClassSpec c{0, 0, 3};
+      c.segs.push_back({0, 0, 64, 1, square_taps(7, 0)});
+      gemm("outconv_7x7", e.W.outc, {{U3, 1, false}}, {c}, 64, B, H, W,
+           OutSpec{OUT_F32_NCHW, out, 0, 3, H, W, 0, 0, nullptr}, 0, 1, 2.0 * B * H * W * 3 * 3136, 16);
+    }
+  }
+};
+
+void check_device_error(lama_engine* e) {
+  int v = 0;
+  CK(cudaMemcpy(&v, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v != 0) {
+    cudaMemset(e->d_err, 0, sizeof(int));
+    throw EngineError{LAMA_EDEVICE, "a kernel wait timed out on the device (code " + std::to_string(v) + ")"};
+  }
+}
+
+Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int nblocks) {
+  auto key = std::make_tuple(kind, B, H, W, h, w, nblocks);
+  auto it = e->plans.find(key);
+  if (it != e->plans.end()) return *it->second;
+  std::unique_ptr<Plan> pl(new Plan());
+  pl->kind = kind; pl->B = B; pl->H = H; pl->W = W; pl->h = h; pl->w = w; pl->nblocks = nblocks;
+  Builder b{*e, *pl};
+  if (kind == 0 || kind == 1) {
+    Act U = b.act(B, H + 6, W, 32, 0);
+    pl->out = (float*)pl->mem.alloc((size_t)B * 3 * H * W * 4);
+    Op un;
+    un.name = "unfold_input";
+    un.u.batch = B; un.u.H = H; un.u.W = W; un.u.h = h; un.u.w = w;
+    un.u.out = U.p;
+    un.u.out_part = U.part();
+    un.out_ptr = U.p; un.out_split = 1; un.out_part = U.part();
+    un.dims[0] = B; un.dims[1] = H + 6; un.dims[2] = W; un.dims[3] = 32;
+    if (kind == 0) {
+      pl->in_f32 = (float*)pl->mem.alloc((size_t)B * 4 * H * W * 4);
+      un.kind = OP_UNFOLD_F32;
+      un.u.in = pl->in_f32;
+    } else {
+      pl->rgb = (uint8_t*)pl->mem.alloc((size_t)B * h * w * 3);
+      pl->mask = (uint8_t*)pl->mem.alloc((size_t)B * h * w);
+      pl->out_rgb = (uint8_t*)pl->mem.alloc((size_t)B * h * w * 3);
+      un.kind = OP_UNFOLD_U8;
+      un.u.rgb = pl->rgb;
+      un.u.mask = pl->mask;
+    }
+    pl->ops.push_back(std::move(un));
+    b.core(U, B, H, W, pl->out);
+    if (kind == 1) {
+      Op c;
+      c.kind = OP_COMPOSITE;
+      c.name = "composite";
+      c.c = CompositeParams{B, h, w, H, W, pl->rgb, pl->mask, pl->out, pl->out_rgb};
+      pl->ops.push_back(std::move(c));
+    }
+  } else {
+    Act XA = b.act(B, H, W, 512, 1);
+    Act XB = b.act(B, H, W, 512, 1);
+    pl->l_in = (float*)pl->mem.alloc((size_t)B * 128 * H * W * 4);
+    pl->g_in = (float*)pl->mem.alloc((size_t)B * 384 * H * W * 4);
+    pl->l_out = (float*)pl->mem.alloc((size_t)B * 128 * H * W * 4);
+    pl->g_out = (float*)pl->mem.alloc((size_t)B * 384 * H * W * 4);
+    for (int i = 0; i < 2; i++) {
+      Op cv;
+      cv.kind = OP_TO_SPLIT;
+      cv.name = "nchw_to_split";
+      cv.cv = ConvertParams{B, i == 0 ? 128 : 384, H, W, 1, 512, i == 0 ? 0 : 128, i == 0 ? pl->l_in : pl->g_in,
+                            XA.p, XA.part()};
+      pl->ops.push_back(std::move(cv));
+    }
+    b.resblocks(XA, XB, nblocks);
+    for (int i = 0; i < 2; i++) {
+      Op cv;
+      cv.kind = OP_TO_NCHW;
+      cv.name = "split_to_nchw";
+      cv.cv = ConvertParams{B, i == 0 ? 128 : 384, H, W, 1, 512, i == 0 ? 0 : 128,
+                            i == 0 ? pl->l_out : pl->g_out, XA.p, XA.part()};
+      pl->ops.push_back(std::move(cv));
+    }
+  }
+  // Capture the pass into a CUDA graph.
+  cudaGraph_t graph = nullptr;
+  CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  int lerr = 0;
+  for (const Op& op : pl->ops) {
+    lerr = launch_op(op, e->stream);
+    if (lerr) break;
+  }
+  cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
+  if (lerr) {
+    if (graph) cudaGraphDestroy(graph);
+    throw EngineError{LAMA_ECUDA, std::string("kernel launch during capture: ") + cudaGetErrorString((cudaError_t)lerr)};
+  }
+  CK(ce);
+  cudaError_t ie = cudaGraphInstantiate(&pl->exec, graph, 0);
+  cudaGraphDestroy(graph);
+  CK(ie);
+  Plan& ref = *pl;
+  e->plans[key] = std::move(pl);
+  return ref;
+}
+
+void run_plan(lama_engine* e, Plan& pl) { CK(cudaGraphLaunch(pl.exec, e->stream)); }
+
+void sync_check(lama_engine* e) {
+  CK(cudaStreamSynchronize(e->stream));
+  check_device_error(e);
+}
+
+template <class F>
+int guarded(lama_engine* e, F&& f) {
+  if (!e) return LAMA_EINVAL;
+  try {
+    CK(cudaSetDevice(e->device));
+    f();
+    e->err.clear();
+    return LAMA_OK;
+  } catch (const EngineError& x) {
+    e->err = x.msg;
+    return x.code;
+  } catch (const std::exception& x) {
+    e->err = x.what();
+    return LAMA_EINVAL;
+  }
+}
+
+void check_shape(int batch, int h, int w, bool mult8) {
+  if (batch < 1 || h < 1 || w < 1) throw EngineError{LAMA_EINVAL, "batch, h and w must be positive"};
+  if (mult8 && (h % 8 || w % 8))
+    throw EngineError{LAMA_EINVAL, "h and w must be multiples of 8 (the generator has three stride-2 stages)"};
+}
+
+}  // namespace
+
+extern "C" {
+
+int lama_abi_version(void) { return 1; }
+
+int lama_open(const char* weights_path, int device, lama_engine** out) {
+  if (!out) return LAMA_EINVAL;
+  *out = nullptr;
+  lama_engine* e = new lama_engine();
+  e->device = device;
+  *out = e;
+  if (!weights_path) {
+    e->err = "weights path is null";
+    return LAMA_EINVAL;
+  }
+  return guarded(e, [&] {
+    int ndev = 0;
+    CK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev)
+      throw EngineError{LAMA_EINVAL, "device " + std::to_string(device) + " does not exist (" + std::to_string(ndev) +
+                                         " visible)"};
+    CK(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+      throw EngineError{LAMA_EUNSUPPORTED, std::string("this engine is built for sm_100a (B200); device is ") +
+                                               prop.name + " sm_" + std::to_string(prop.major) +
+                                               std::to_string(prop.minor)};
+    e->sms = prop.multiProcessorCount;
+    CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    CKL(conv_gemm_prepare());
+    CKL(fft_prepare(200 * 1024 + 4096));
+    e->d_err = (int*)e->wmem.alloc(256);
+    WeightFile wf;
+    std::string err;
+    if (!wf.open(weights_path, err)) throw EngineError{LAMA_EWEIGHTS, err};
+    load_weights(wf, e->wmem, e->W);
+  });
+}
+
+int lama_forward(lama_engine* e, const float* in, int batch, int h, int w, float* out) {
+  return guarded(e, [&] {
+    if (!in || !out) throw EngineError{LAMA_EINVAL, "null buffer"};
+    check_shape(batch, h, w, true);
+    Plan& pl = get_plan(e, 0, batch, h, w, h, w, 18);
+    const size_t nin = (size_t)batch * 4 * h * w, nout = (size_t)batch * 3 * h * w;
+    CK(cudaMemcpyAsync(pl.in_f32, in, nin * 4, cudaMemcpyHostToDevice, e->stream));
+    run_plan(e, pl);
+    CK(cudaMemcpyAsync(out, pl.out, nout * 4, cudaMemcpyDeviceToHost, e->stream));
+    sync_check(e);
+  });
+}
+
+int lama_forward_device(lama_engine* e, const float* d_in, int batch, int h, int w, float* d_out) {
+  return guarded(e, [&] {
+    if (!d_in || !d_out) throw EngineError{LAMA_EINVAL, "null buffer"};
+    check_shape(batch, h, w, true);
+    Plan& pl = get_plan(e, 0, batch, h, w, h, w, 18);
+    const size_t nin = (size_t)batch * 4 * h * w, nout = (size_t)batch * 3 * h * w;
+    CK(cudaMemcpyAsync(pl.in_f32, d_in, nin * 4, cudaMemcpyDeviceToDevice, e->stream));
+    run_plan(e, pl);
+    CK(cudaMemcpyAsync(d_out, pl.out, nout * 4, cudaMemcpyDeviceToDevice, e->stream));
+  });
+}
+
+int lama_inpaint_u8(lama_engine* e, const uint8_t* rgb, const uint8_t* mask, int batch, int h, int w,
+                    uint8_t* out_rgb) {
+  return guarded(e, [&] {
+    if (!rgb || !mask || !out_rgb) throw EngineError{LAMA_EINVAL, "null buffer"};
+    check_shape(batch, h, w, false);
+    const int H = (h + 7) / 8 * 8, W = (w + 7) / 8 * 8;
+    Plan& pl = get_plan(e, 1, batch, H, W, h, w, 18);
+    const size_t npx = (size_t)batch * h * w;
+    CK(cudaMemcpyAsync(pl.rgb, rgb, npx * 3, cudaMemcpyHostToDevice, e->stream));
+    CK(cudaMemcpyAsync(pl.mask, mask, npx, cudaMemcpyHostToDevice, e->stream));
+    run_plan(e, pl);
+    CK(cudaMemcpyAsync(out_rgb, pl.out_rgb, npx * 3, cudaMemcpyDeviceToHost, e->stream));
+    sync_check(e);
+  });
+}
+
+int lama_inpaint_u8_device(lama_engine* e, const uint8_t* d_rgb, const uint8_t* d_mask, int batch, int h, int w,
+                           uint8_t* d_out_rgb) {
+  return guarded(e, [&] {
+    if (!d_rgb || !d_mask || !d_out_rgb) throw EngineError{LAMA_EINVAL, "null buffer"};
+    check_shape(batch, h, w, false);
+    const int H = (h + 7) / 8 * 8, W = (w + 7) / 8 * 8;
+    Plan& pl = get_plan(e, 1, batch, H, W, h, w, 18);
+    const size_t npx = (size_t)batch * h * w;
+    CK(cudaMemcpyAsync(pl.rgb, d_rgb, npx * 3, cudaMemcpyDeviceToDevice, e->stream));
+    CK(cudaMemcpyAsync(pl.mask, d_mask, npx, cudaMemcpyDeviceToDevice, e->stream));
+    run_plan(e, pl);
+    CK(cudaMemcpyAsync(d_out_rgb, pl.out_rgb, npx * 3, cudaMemcpyDeviceToDevice, e->stream));
+  });
+}
+
+static int resblocks_impl(lama_engine* e, const float* l_in, const float* g_in, int batch, int h, int w, int nblocks,
+                          float* l_out, float* g_out, cudaMemcpyKind kin, cudaMemcpyKind kout, bool sync) {
+  return guarded(e, [&] {
+    if (!l_in || !g_in || !l_out || !g_out) throw EngineError{LAMA_EINVAL, "null buffer"};
+    check_shape(batch, h, w, false);
+    if (nblocks < 0 || nblocks > 18) throw EngineError{LAMA_EINVAL, "nblocks must be in 0..18"};
+    Plan& pl = get_plan(e, 2, batch, h, w, h, w, nblocks);
+    const size_t nl = (size_t)batch * 128 * h * w, ng = (size_t)batch * 384 * h * w;
+    CK(cudaMemcpyAsync(pl.l_in, l_in, nl * 4, kin, e->stream));
+    CK(cudaMemcpyAsync(pl.g_in, g_in, ng * 4, kin, e->stream));
+    run_plan(e, pl);
+    CK(cudaMemcpyAsync(l_out, pl.l_out, nl * 4, kout, e->stream));
+    CK(cudaMemcpyAsync(g_out, pl.g_out, ng * 4, kout, e->stream));
+    if (sync) sync_check(e);
+  });
+}
+
+int lama_resblocks(lama_engine* e, const float* local_in, const float* global_in, int batch, int h, int w,
+                   int nblocks, float* local_out, float* global_out) {
+  return resblocks_impl(e, local_in, global_in, batch, h, w, nblocks, local_out, global_out, cudaMemcpyHostToDevice,
+                        cudaMemcpyDeviceToHost, true);
+}
+
+int lama_resblocks_device(lama_engine* e, const float* d_local_in, const float* d_global_in, int batch, int h,
+                          int w, int nblocks, float* d_local_out, float* d_global_out) {
+  return resblocks_impl(e, d_local_in, d_global_in, batch, h, w, nblocks, d_local_out, d_global_out,
+                        cudaMemcpyDeviceToDevice, cudaMemcpyDeviceToDevice, false);
+}
+
+const char* lama_last_error(const lama_engine* e) { return e ? e->err.c_str() : "null engine"; }
+
+int lama_synchronize(lama_engine* e) {
+  return guarded(e, [&] { sync_check(e); });
+}
+
+void* lama_stream(lama_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+int lama_launch_count(lama_engine* e, int batch, int h, int w) {
+  int n = 0;
+  int rc = guarded(e, [&] {
+    check_shape(batch, h, w, true);
+    n = (int)get_plan(e, 0, batch, h, w, h, w, 18).ops.size();
+  });
+  return rc ? rc : n;
+}
+
+int lama_profile_forward(lama_engine* e, const float* d_in, int batch, int h, int w, float* d_out,
+                         lama_kernel_stat* stats, int max_stats, int* n_stats) {
+  return guarded(e, [&] {
+    check_shape(batch, h, w, true);
+    Plan& pl = get_plan(e, 0, batch, h, w, h, w, 18);
+    const size_t nin = (size_t)batch * 4 * h * w, nout = (size_t)batch * 3 * h * w;
+    CK(cudaMemcpyAsync(pl.in_f32, d_in, nin * 4, cudaMemcpyDeviceToDevice, e->stream));
+    std::vector<cudaEvent_t> ev(pl.ops.size() + 1);
+    for (auto& x : ev) CK(cudaEventCreate(&x));
+    CK(cudaEventRecord(ev[0], e->stream));
+    for (size_t i = 0; i < pl.ops.size(); i++) {
+      CKL(launch_op(pl.ops[i], e->stream));
+      CK(cudaEventRecord(ev[i + 1], e->stream));
+    }
+    CK(cudaMemcpyAsync(d_out, pl.out, nout * 4, cudaMemcpyDeviceToDevice, e->stream));
+    sync_check(e);
+    std::vector<std::string> names;
+    std::map<std::string, lama_kernel_stat> agg;
+    for (size_t i = 0; i < pl.ops.size(); i++) {
+      float ms = 0;
+      CK(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+      const std::string& nm = pl.ops[i].name;
+      if (!agg.count(nm)) {
+        lama_kernel_stat s{};
+        snprintf(s.name, sizeof(s.name), "%s", nm.c_str());
+        agg[nm] = s;
+        names.push_back(nm);
+      }
+      lama_kernel_stat& s = agg[nm];
+      s.launches++;
+      s.ms += ms;
+      s.flops += pl.ops[i].flops;
+      s.bytes += pl.ops[i].bytes;
+    }
+    for (auto& x : ev) cudaEventDestroy(x);
+    int n = 0;
+    for (const std::string& nm : names) {
+      if (n < max_stats && stats) stats[n] = agg[nm];
+      n++;
+    }
+    if (n_stats) *n_stats = n;
+  });
+}
+
+int lama_debug_run(lama_engine* e, const float* in, int batch, int h, int w, int n_ops) {
+  return guarded(e, [&] {
+    check_shape(batch, h, w, true);
+    Plan& pl = get_plan(e, 0, batch, h, w, h, w, 18);
+    CK(cudaMemcpyAsync(pl.in_f32, in, (size_t)batch * 4 * h * w * 4, cudaMemcpyHostToDevice, e->stream));
+    const int n = std::min<int>(n_ops, (int)pl.ops.size());
+    for (int i = 0; i < n; i++) CKL(launch_op(pl.ops[i], e->stream));
+    sync_check(e);
+  });
+}
+
+int lama_debug_read(lama_engine* e, int batch, int h, int w, int op, float* out, long long cap, int* dims,
+                    char* name) {
+  return guarded(e, [&] {
+    Plan& pl = get_plan(e, 0, batch, h, w, h, w, 18);
+    if (op < 0 || op >= (int)pl.ops.size()) throw EngineError{LAMA_EINVAL, "op index out of range"};
+    const Op& o = pl.ops[op];
+    if (!o.out_ptr) throw EngineError{LAMA_EINVAL, "op has no recorded output"};
+    const long long n = (long long)o.dims[0] * o.dims[1] * o.dims[2] * o.dims[3];
+    for (int i = 0; i < 4; i++) dims[i] = o.dims[i];
+    if (name) snprintf(name, 32, "%s", o.name.c_str());
+    if (!out) return;
+    if (n > cap) throw EngineError{LAMA_EINVAL, "buffer too small"};
+    if (o.out_split) {
+      std::vector<uint16_t> hl((size_t)2 * n);
+      CK(cudaMemcpy(hl.data(), o.out_ptr, (size_t)n * 2, cudaMemcpyDeviceToHost));
+      CK(cudaMemcpy(hl.data() + n, (uint16_t*)o.out_ptr + o.out_part, (size_t)n * 2, cudaMemcpyDeviceToHost));
+      for (long long i = 0; i < n; i++) out[i] = bf2f(hl[i]) + bf2f(hl[n + i]);
+    } else {
+      CK(cudaMemcpy(out, o.out_ptr, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    }
+  });
+}
+
+void lama_close(lama_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  e->plans.clear();
+  e->wmem.free_all();
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+}  // extern "C"

@@ -1,0 +1,90 @@
+// Parameter block of the implicit-GEMM convolution kernel (conv_gemm.cu).
+//
+// One launch computes  out[pixel][n] = epilogue( sum_k A[pixel][k] * B[n][k] )
+// over one or more "tile classes".  A class owns a range of output channels
+// and its own K list; K is a concatenation of segments, each a convolution
+// (a list of taps) over a channel range of one activation tensor.  This is
+// how one launch expresses:
+//   * a plain KxK convolution (one class, one segment),
+//   * an FFC layer's two outputs with concatenated K (local: 3x3 over all 512
+//     channels = l2l|g2l; global: 3x3 over the 128 local channels then the
+//     1x1 spectral conv2 = l2g|conv2), as two classes of one launch,
+//   * a stride-2 transposed convolution as its four output phases (four
+//     classes with 1, 2, 2, 4 taps and strided output placement).
+//
+// Activations are NHWC and carried as split bf16 pairs: a buffer
+// [2][B][H+2h][W+2h][C] holds hi = bf16(v) in part 0 and lo = bf16(v - hi)
+// in part 1, with an optional halo h of reflected pixels.  A tensor maps
+// address them as 5-D (C, Wp, Hp, B, part).  Weights are [2][N][K] bf16
+// (hi/lo), addressed as 3-D (K, N, part).
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+namespace lama {
+
+constexpr int GEMM_MAX_TAPS = 49;
+constexpr int GEMM_MAX_SEGS = 2;
+constexpr int GEMM_MAX_CLASSES = 4;
+constexpr int GEMM_MAX_AMAPS = 3;
+
+enum OutKind : int {
+  OUT_SPLIT = 0,     // split bf16 NHWC (optionally halo'd, reflect-filled)
+  OUT_F32_NHWC = 1,  // fp32 NHWC
+  OUT_F32_NCHW = 2,  // fp32 NCHW, channels < nvalid only
+};
+
+struct GemmSeg {
+  int amap;    // index into GemmParams::amap
+  int c0;      // first channel of this segment in the A tensor
+  int nblk;    // CB-channel blocks per tap
+  int ntaps;   // taps
+  int stride;  // the tile origin is multiplied by this in A coordinates
+  int sub0;    // index of the segment's first A sub-box within its class
+  int8_t dy[GEMM_MAX_TAPS];  // tap offsets in A map coordinates
+  int8_t dx[GEMM_MAX_TAPS];
+};
+
+struct GemmClass {
+  int n0;        // first output channel (absolute, indexes scale/shift and out)
+  int nvalid;    // output channels in this class
+  int ntiles_n;  // BN-wide tiles covering nvalid
+  int nkb;       // 64-wide K blocks
+  int nseg;
+  int oy_mul, oy_add, ox_mul, ox_add;  // output pixel = M pixel * mul + add
+  int tile0;     // first global tile index of the class
+  GemmSeg seg[GEMM_MAX_SEGS];
+};
+
+struct GemmParams {
+  CUtensorMap amap[GEMM_MAX_AMAPS];
+  CUtensorMap bmap[GEMM_MAX_CLASSES];
+  GemmClass cls[GEMM_MAX_CLASSES];
+  int nclass;
+  int cb;                     // channels per A sub-box: 64 (128B swizzle) or 32 (64B swizzle)
+  int batch, mh, mw;          // M space: images x rows x cols
+  int bh, bw;                 // tile rows x cols, bh * bw == 128
+  int tiles_y, tiles_x, m_tiles;
+  int total_tiles;
+  // epilogue
+  const float* scale;         // per absolute output channel
+  const float* shift;
+  int relu;
+  int sigmoid;
+  int out_kind;
+  void* out;
+  long long out_part;         // elements per part of a split output
+  int out_c, out_h, out_w;    // output tensor channels and interior extent
+  int out_halo, out_reflect;  // halo width; fill it by reflection
+  const void* skip;           // split residual, same geometry as out (may alias it)
+  int* err;                   // device status word (0 = ok)
+};
+
+// Host launcher (conv_gemm.cu).  `bn` in {16, 64, 128, 192, 256}.
+int launch_conv_gemm(const GemmParams& p, int bn, int grid, cudaStream_t stream);
+size_t conv_gemm_smem_bytes(int bn);
+int conv_gemm_stages(int bn);
+int conv_gemm_prepare();
+
+}  // namespace lama

@@ -1,0 +1,219 @@
+"""ctypes binding of the B200 engine (liblama_b200.so, include/lama_b200.h).
+
+This is the Python face of the reference's operator boundary:
+
+* `Engine(weights, device)`  ~ `WeightStore::open` + `cuda::load_steps`
+  (lama-rs/src/weights.rs:80-106, lama-rs/src/cuda.rs:903-962);
+* `Engine.forward(x)`        ~ `cuda::run` / `infer` (lama-rs/src/cuda.rs:1542-1691,
+  lama-rs/src/main.rs:318-361): [4,h,w] or [B,4,h,w] f32 in, [3,h,w] / [B,3,h,w] out;
+* `Engine.inpaint_u8(rgb, mask)` ~ `build_input` + `infer` + composite
+  (lama-rs/src/main.rs:175-196, 272-307).
+
+Errors raise `LamaError` carrying the engine's message (the reference's
+`Err(String)`).  There is no CPU fallback: if the native library cannot be
+loaded, importing the engine raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.environ.get("LAMA_B200_LIB", os.path.join(PKG_ROOT, "liblama_b200.so"))
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_vp = ctypes.c_void_p
+
+LAMA_ERRORS = {-1: "EINVAL", -2: "EWEIGHTS", -3: "ECUDA", -4: "EDEVICE", -5: "ENOMEM", -6: "EUNSUPPORTED"}
+
+
+class LamaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{LAMA_ERRORS.get(code, code)}: {msg}")
+        self.code = code
+        self.msg = msg
+
+
+class KernelStat(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 32), ("launches", ctypes.c_int), ("ms", ctypes.c_double),
+                ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
+
+
+_lib = None
+
+# Every symbol include/lama_b200.h declares: (name, restype, argtypes).
+SIGNATURES = [
+    ("lama_abi_version", ctypes.c_int, []),
+    ("lama_open", ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(_vp)]),
+    ("lama_forward", ctypes.c_int, [_vp, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]),
+    ("lama_forward_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    ("lama_inpaint_u8", ctypes.c_int, [_vp, _u8p, _u8p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _u8p]),
+    ("lama_inpaint_u8_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    ("lama_resblocks", ctypes.c_int, [_vp, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      _f32p, _f32p]),
+    ("lama_resblocks_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int, _vp, _vp]),
+    ("lama_last_error", ctypes.c_char_p, [_vp]),
+    ("lama_synchronize", ctypes.c_int, [_vp]),
+    ("lama_stream", _vp, [_vp]),
+    ("lama_launch_count", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    ("lama_profile_forward", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp,
+                                            ctypes.POINTER(KernelStat), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    ("lama_debug_run", ctypes.c_int, [_vp, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    ("lama_debug_read", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p,
+                                       ctypes.c_longlong, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p]),
+    ("lama_close", None, [_vp]),
+]
+
+
+def lib():
+    """Load liblama_b200.so (raises OSError if it is missing: no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is missing: build it with `make -C lama-inpaint-rs_b200/csrc` "
+                          "(the engine has no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, res, args in SIGNATURES:
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _fp(a):
+    return a.ctypes.data_as(_f32p)
+
+
+def _up(a):
+    return a.ctypes.data_as(_u8p)
+
+
+class Engine:
+    def __init__(self, weights_path: str, device: int = 0):
+        L = lib()
+        h = _vp()
+        rc = L.lama_open(os.fsencode(weights_path), device, ctypes.byref(h))
+        self._h = h
+        if rc != 0:
+            msg = L.lama_last_error(h).decode() if h else ""
+            L.lama_close(h)
+            self._h = None
+            raise LamaError(rc, msg)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().lama_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def _check(self, rc):
+        if rc != 0:
+            raise LamaError(rc, lib().lama_last_error(self._h).decode())
+
+    @property
+    def handle(self):
+        return self._h
+
+    def stream(self) -> int:
+        return lib().lama_stream(self._h) or 0
+
+    def synchronize(self):
+        self._check(lib().lama_synchronize(self._h))
+
+    # -------------------------------------------------------------- forward
+    def forward(self, x: np.ndarray) -> np.ndarray:
+        """x: [4,h,w] or [B,4,h,w] f32 -> sigmoid output [3,h,w] / [B,3,h,w]."""
+        x = np.ascontiguousarray(x, np.float32)
+        single = x.ndim == 3
+        if single:
+            x = x[None]
+        b, c, h, w = x.shape
+        if c != 4:
+            raise LamaError(-1, f"input must have 4 channels, got {c}")
+        out = np.empty((b, 3, h, w), np.float32)
+        self._check(lib().lama_forward(self._h, _fp(x), b, h, w, _fp(out)))
+        return out[0] if single else out
+
+    def forward_device(self, d_in: int, d_out: int, batch: int, h: int, w: int):
+        """Device pointers (e.g. torch data_ptr()); queued on the engine stream."""
+        self._check(lib().lama_forward_device(self._h, d_in, batch, h, w, d_out))
+
+    def inpaint_u8(self, rgb: np.ndarray, mask: np.ndarray) -> np.ndarray:
+        """rgb [h,w,3] / [B,h,w,3] u8, mask [h,w] / [B,h,w] u8 -> composited u8 RGB."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        mask = np.ascontiguousarray(mask, np.uint8)
+        single = rgb.ndim == 3
+        if single:
+            rgb, mask = rgb[None], mask[None]
+        b, h, w, _ = rgb.shape
+        if mask.shape != (b, h, w):
+            raise LamaError(-1, f"mask is {mask.shape[-1]}x{mask.shape[-2]} but image is {w}x{h}")
+        out = np.empty_like(rgb)
+        self._check(lib().lama_inpaint_u8(self._h, _up(rgb), _up(mask), b, h, w, _up(out)))
+        return out[0] if single else out
+
+    def inpaint_u8_device(self, d_rgb: int, d_mask: int, d_out: int, batch: int, h: int, w: int):
+        self._check(lib().lama_inpaint_u8_device(self._h, d_rgb, d_mask, batch, h, w, d_out))
+
+    def resblocks(self, local: np.ndarray, glob: np.ndarray, nblocks: int = 18):
+        """The 18-block FFC stack: local [B,128,h,w], global [B,384,h,w] f32."""
+        l = np.ascontiguousarray(local, np.float32)
+        g = np.ascontiguousarray(glob, np.float32)
+        single = l.ndim == 3
+        if single:
+            l, g = l[None], g[None]
+        b, _, h, w = l.shape
+        lo = np.empty_like(l)
+        go = np.empty_like(g)
+        self._check(lib().lama_resblocks(self._h, _fp(l), _fp(g), b, h, w, nblocks, _fp(lo), _fp(go)))
+        return (lo[0], go[0]) if single else (lo, go)
+
+    def resblocks_device(self, d_l, d_g, d_lo, d_go, batch, h, w, nblocks=18):
+        self._check(lib().lama_resblocks_device(self._h, d_l, d_g, batch, h, w, nblocks, d_lo, d_go))
+
+    def launch_count(self, batch: int, h: int, w: int) -> int:
+        n = lib().lama_launch_count(self._h, batch, h, w)
+        if n < 0:
+            self._check(n)
+        return n
+
+    def profile_forward(self, d_in: int, d_out: int, batch: int, h: int, w: int):
+        stats = (KernelStat * 64)()
+        n = ctypes.c_int(0)
+        self._check(lib().lama_profile_forward(self._h, d_in, batch, h, w, d_out, stats, 64, ctypes.byref(n)))
+        return [dict(name=s.name.decode(), launches=s.launches, ms=s.ms, flops=s.flops, bytes=s.bytes)
+                for s in stats[: n.value]]
+
+    # -------------------------------------------------------------- diagnostics
+    def debug_run(self, x: np.ndarray, n_ops: int):
+        x = np.ascontiguousarray(x, np.float32)
+        if x.ndim == 3:
+            x = x[None]
+        b, _, h, w = x.shape
+        self._check(lib().lama_debug_run(self._h, _fp(x), b, h, w, n_ops))
+
+    def debug_read(self, batch: int, h: int, w: int, op: int):
+        dims = (ctypes.c_int * 4)()
+        name = ctypes.create_string_buffer(32)
+        self._check(lib().lama_debug_read(self._h, batch, h, w, op, None, 0, dims, name))
+        n = dims[0] * dims[1] * dims[2] * dims[3]
+        out = np.empty(n, np.float32)
+        self._check(lib().lama_debug_read(self._h, batch, h, w, op, _fp(out), n, dims, name))
+        return name.value.decode(), out.reshape(tuple(dims))
