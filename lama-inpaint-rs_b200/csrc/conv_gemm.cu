@@ -36,6 +36,10 @@ __host__ __device__ constexpr int stages_for(int bn) {
   // (2 * A_PART + 2 * bn * 128) bytes per stage, within ~200 KB
   return bn <= 16 ? 5 : bn <= 64 ? 4 : bn <= 128 ? 3 : 2;
 }
+// Extra shared memory of the shifted-sum epilogue (OUT_SHIFT7_NCHW):
+// two 128 x 33 fp32 staging tiles.
+constexpr int SHIFT_LD = 33;
+__host__ __device__ constexpr uint32_t extra_smem(int bn) { return bn == 32 ? 2u * 128u * SHIFT_LD * 4u : 0u; }
 __host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 2 * A_PART + 2u * (uint32_t)bn * 128u; }
 __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
   return 2 * bn <= 32 ? 32 : 2 * bn <= 64 ? 64 : 2 * bn <= 128 ? 128 : 2 * bn <= 256 ? 256 : 512;
@@ -58,7 +62,7 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
   ti.b = mt / per_img;
   int r = mt - ti.b * per_img;
   ti.i0 = (r / p.tiles_x) * p.bh;
-  ti.j0 = (r % p.tiles_x) * p.bw;
+  ti.j0 = (r % p.tiles_x) * p.step_x;
   return ti;
 }
 
@@ -177,6 +181,7 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  float* shift_buf = reinterpret_cast<float*>(smem + STAGES * STAGE + 256);
   const uint32_t smem0 = smem_u32(smem);
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
@@ -298,6 +303,33 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
       const bool valid = (i < p.mh) && (j < p.mw);
       const int oy = i * C.oy_mul + C.oy_add, ox = j * C.ox_mul + C.ox_add;
       const uint32_t trow = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr (BN == 32) {
+        if (p.out_kind == OUT_SHIFT7_NCHW) {
+          float v[32];
+          tmem_ld32(trow, v);
+          tmem_wait_ld();
+          float* P = shift_buf + (it & 1) * 128 * SHIFT_LD;
+#pragma unroll
+          for (int k = 0; k < 32; k++) P[m * SHIFT_LD + k] = v[k];
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const int x = ti.j0 + m;
+          if (m < p.step_x && x < p.out_w && i < p.mh) {
+#pragma unroll
+            for (int co = 0; co < 3; co++) {
+              float acc = 0.f;
+#pragma unroll
+              for (int kx = 0; kx < 7; kx++) acc += P[(m + kx) * SHIFT_LD + kx * 4 + co];
+              const float z = acc + __ldg(p.shift + co);
+              const float e = expf(-z);
+              reinterpret_cast<float*>(p.out)[(((long long)ti.b * p.out_c + co) * p.out_h + i) * p.out_w + x] =
+                  1.0f / (1.0f + e);
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(tempty_bar(acc));
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int ch = 0; ch < BN / CH; ch++) {
         float v[CH];
@@ -321,20 +353,20 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
 
 template <int BN>
 int prepare_bn() {
-  const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256;
+  const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256 + extra_smem(BN);
   return (int)cudaFuncSetAttribute(k_conv_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 
 template <int BN>
 int launch_bn(const GemmParams& p, int grid, cudaStream_t stream) {
-  const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256;
+  const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256 + extra_smem(BN);
   k_conv_gemm<BN><<<grid, 256, smem, stream>>>(p);
   return (int)cudaGetLastError();
 }
 
 }  // namespace
 
-size_t conv_gemm_smem_bytes(int bn) { return (size_t)stages_for(bn) * stage_bytes(bn) + 1024 + 256; }
+size_t conv_gemm_smem_bytes(int bn) { return (size_t)stages_for(bn) * stage_bytes(bn) + 1024 + 256 + extra_smem(bn); }
 int conv_gemm_stages(int bn) { return stages_for(bn); }
 
 // Opt every tile width into its dynamic shared memory size on the current
@@ -342,6 +374,7 @@ int conv_gemm_stages(int bn) { return stages_for(bn); }
 int conv_gemm_prepare() {
   int e = 0;
   if ((e = prepare_bn<16>())) return e;
+  if ((e = prepare_bn<32>())) return e;
   if ((e = prepare_bn<64>())) return e;
   if ((e = prepare_bn<128>())) return e;
   if ((e = prepare_bn<192>())) return e;
@@ -351,6 +384,7 @@ int conv_gemm_prepare() {
 int launch_conv_gemm(const GemmParams& p, int bn, int grid, cudaStream_t stream) {
   switch (bn) {
     case 16: return launch_bn<16>(p, grid, stream);
+    case 32: return launch_bn<32>(p, grid, stream);
     case 64: return launch_bn<64>(p, grid, stream);
     case 128: return launch_bn<128>(p, grid, stream);
     case 192: return launch_bn<192>(p, grid, stream);

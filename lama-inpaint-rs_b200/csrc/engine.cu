@@ -152,13 +152,15 @@ CUtensorMap act_map(const Act& a, int cb, int bw, int bh, int stride, bool inter
 // ------------------------------------------------------------------ weights
 struct WClass {
   int n = 0, npad = 0, k = 0;
-  void* w = nullptr;  // [2][npad][k] bf16
+  void* w = nullptr;            // [2][npad][k] bf16 on the device
+  std::vector<uint16_t> host;   // staged until the device exists
 };
 
 struct GemmW {
   std::vector<WClass> cls;
   float* scale = nullptr;
   float* shift = nullptr;
+  std::vector<float> hscale, hshift;
   int nout = 0;
 };
 
@@ -189,7 +191,6 @@ struct Weights {
 
 struct Loader {
   const WeightFile& wf;
-  DevMem& mem;
   std::vector<float> get(const std::string& name, const std::vector<int64_t>& shape) {
     std::vector<float> v;
     std::string err;
@@ -223,18 +224,53 @@ struct Loader {
         h[(size_t)i * k + j] = hi;
         h[(size_t)c.npad * k + (size_t)i * k + j] = lo;
       }
-    c.w = mem.alloc(h.size() * 2, false);
-    CK(cudaMemcpy(c.w, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+    c.host = std::move(h);
     return c;
   }
   void affine(GemmW& g, const std::vector<float>& s, const std::vector<float>& t) {
     g.nout = (int)s.size();
-    g.scale = (float*)mem.alloc(s.size() * 4, false);
-    g.shift = (float*)mem.alloc(t.size() * 4, false);
-    CK(cudaMemcpy(g.scale, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(g.shift, t.data(), t.size() * 4, cudaMemcpyHostToDevice));
+    g.hscale = s;
+    g.hshift = t;
   }
 };
+
+// Copy every staged weight matrix and affine vector into one device arena.
+void upload_gemm(GemmW& g, char*& cur) {
+  for (WClass& c : g.cls) {
+    c.w = cur;
+    CK(cudaMemcpy(c.w, c.host.data(), c.host.size() * 2, cudaMemcpyHostToDevice));
+    cur += (c.host.size() * 2 + 255) / 256 * 256;
+    c.host.clear();
+    c.host.shrink_to_fit();
+  }
+  g.scale = (float*)cur;
+  CK(cudaMemcpy(g.scale, g.hscale.data(), g.hscale.size() * 4, cudaMemcpyHostToDevice));
+  cur += (g.hscale.size() * 4 + 255) / 256 * 256;
+  g.shift = (float*)cur;
+  CK(cudaMemcpy(g.shift, g.hshift.data(), g.hshift.size() * 4, cudaMemcpyHostToDevice));
+  cur += (g.hshift.size() * 4 + 255) / 256 * 256;
+}
+
+size_t gemm_bytes(const GemmW& g) {
+  size_t b = 0;
+  for (const WClass& c : g.cls) b += (c.host.size() * 2 + 255) / 256 * 256;
+  return b + 2 * ((g.hscale.size() * 4 + 255) / 256 * 256);
+}
+
+template <class F>
+void for_each_gemm(Weights& W, F&& f) {
+  f(W.m1); f(W.m2); f(W.m3); f(W.m4);
+  for (FfcW& x : W.ffc) { f(x.conv1); f(x.fu); f(x.out); }
+  for (GemmW& g : W.ct) f(g);
+  f(W.outc);
+}
+
+void upload_weights(Weights& W, DevMem& mem) {
+  size_t total = 0;
+  for_each_gemm(W, [&](GemmW& g) { total += gemm_bytes(g); });
+  char* cur = (char*)mem.alloc(total, false);
+  for_each_gemm(W, [&](GemmW& g) { upload_gemm(g, cur); });
+}
 
 // K order of a kxk conv segment: tap-major (ky, kx), then input channel.
 void put_conv(std::vector<float>& m, int ktot, int kofs, const std::vector<float>& w, int cout, int cin, int kk,
@@ -245,8 +281,10 @@ void put_conv(std::vector<float>& m, int ktot, int kofs, const std::vector<float
         m[(size_t)(row0 + n) * ktot + kofs + t * cin + c] = w[((size_t)n * cin + c) * kk * kk + t];
 }
 
-void load_weights(const WeightFile& wf, DevMem& mem, Weights& W) {
-  Loader L{wf, mem};
+// Reads, checks (names and shapes, as the reference's loaders do:
+// cpu.rs:561-616, cuda.rs:832-962) and repacks every tensor on the host.
+void load_weights(const WeightFile& wf, Weights& W) {
+  Loader L{wf};
   std::vector<float> s, t;
   // model.1: 7x7 4->64 valid.  K = 8 row taps x 32, channel = kx*4 + c (28 used).
   {
@@ -357,21 +395,27 @@ void load_weights(const WeightFile& wf, DevMem& mem, Weights& W) {
     for (int n = 0; n < cout; n++) t[n] = bias[n] * s[n] + t[n];
     L.affine(W.ct[u], s, t);
   }
-  // OutConv 7x7 64 -> 3 with bias, over the reflect-padded input
+  // OutConv 7x7 64 -> 3 with bias, over the reflect-padded input.  The seven
+  // x taps go into N (n = kx*4 + co, 28 used of 32) and K = (ky, c) = 448;
+  // the epilogue sums the kx partial products across neighbouring pixels.
   {
     auto w = L.get("model.34.weight", {3, 64, 7, 7});
     auto bias = L.get("model.34.bias", {3});
-    std::vector<float> m((size_t)3 * 49 * 64, 0.f);
-    put_conv(m, 49 * 64, 0, w, 3, 64, 7);
-    W.outc.cls.push_back(L.upload(m, 3, 49 * 64));
-    std::vector<float> one(16, 1.f), sh(16, 0.f);
+    std::vector<float> m((size_t)32 * 448, 0.f);
+    for (int kx = 0; kx < 7; kx++)
+      for (int co = 0; co < 3; co++)
+        for (int ky = 0; ky < 7; ky++)
+          for (int c = 0; c < 64; c++)
+            m[(size_t)(kx * 4 + co) * 448 + ky * 64 + c] = w[(((size_t)co * 64 + c) * 7 + ky) * 7 + kx];
+    W.outc.cls.push_back(L.upload(m, 32, 448));
+    std::vector<float> one(32, 1.f), sh(32, 0.f);
     for (int n = 0; n < 3; n++) sh[n] = bias[n];
     L.affine(W.outc, one, sh);
   }
 }
 
 // ------------------------------------------------------------------ ops
-enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
+enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
 
 struct Op {
   OpKind kind;
@@ -397,6 +441,8 @@ int launch_op(const Op& op, cudaStream_t st) {
     case OP_GEMM: return launch_conv_gemm(*op.g, op.bn, op.grid, st);
     case OP_RFFT: return launch_rfft2(op.f, st);
     case OP_IRFFT: return launch_irfft2(op.f, st);
+    case OP_RFFT_REG: return launch_fft_reg(op.f, false, st);
+    case OP_IRFFT_REG: return launch_fft_reg(op.f, true, st);
     case OP_UNFOLD_F32: return launch_unfold_f32(op.u, st);
     case OP_UNFOLD_U8: return launch_unfold_u8(op.u, st);
     case OP_COMPOSITE: return launch_composite(op.c, st);
@@ -509,7 +555,7 @@ struct Builder {
 
   void gemm(const std::string& name, const GemmW& Wt, const std::vector<AmapSpec>& amaps,
             const std::vector<ClassSpec>& classes, int cb, int B, int mh, int mw, const OutSpec& o, int relu,
-            int sigmoid, double flops, int force_bn = 0) {
+            int sigmoid, double flops, int force_bn = 0, int step_x = 0) {
     Op op;
     op.kind = OP_GEMM;
     op.name = name;
@@ -518,15 +564,16 @@ struct Builder {
     GemmParams& p = *op.g;
     memset(&p, 0, sizeof(p));
     int bh = 1, bw = 128;
-    choose_tile(mh, mw, bh, bw);
+    if (step_x == 0) choose_tile(mh, mw, bh, bw);
     p.cb = cb;
     p.batch = B;
     p.mh = mh;
     p.mw = mw;
     p.bh = bh;
     p.bw = bw;
+    p.step_x = step_x ? step_x : bw;
     p.tiles_y = (mh + bh - 1) / bh;
-    p.tiles_x = (mw + bw - 1) / bw;
+    p.tiles_x = (mw + p.step_x - 1) / p.step_x;
     p.m_tiles = B * p.tiles_y * p.tiles_x;
     std::vector<int> ns;
     for (auto& c : classes) ns.push_back(c.nvalid);
@@ -590,7 +637,7 @@ struct Builder {
     op.out_ptr = o.p;
     op.out_split = o.kind == OUT_SPLIT;
     op.out_part = o.part;
-    if (o.kind == OUT_F32_NCHW) {
+    if (o.kind == OUT_F32_NCHW || o.kind == OUT_SHIFT7_NCHW) {
       op.dims[0] = B; op.dims[1] = o.c; op.dims[2] = o.h; op.dims[3] = o.w;
     } else {
       op.dims[0] = B; op.dims[1] = o.h + 2 * o.halo; op.dims[2] = o.w + 2 * o.halo; op.dims[3] = o.c;
@@ -665,9 +712,10 @@ struct Builder {
         const std::string tag = "b" + std::to_string(blk) + "." + std::to_string(sub + 1);
         // conv1 1x1 384 -> 192 on the global channels, BN, ReLU -> feat (fp32)
         gemm("spectral_conv1", F.conv1, {{Xin, 1, false}}, {one_seg(0, 0, 192, SegSpec{0, 128, 384, 1, {{1, 1}}})}, 64, B, h, w,
-             OutSpec{OUT_F32_NHWC, feat, 0, 192, h, w, 0, 0, nullptr}, 1, 0, 2.0 * px * 192 * 384);
+             OutSpec{OUT_F32_NCHW, feat, 0, 192, h, w, 0, 0, nullptr}, 1, 0, 2.0 * px * 192 * 384);
+        const bool reg = fft_reg_supported(h, w);
         Op r;
-        r.kind = OP_RFFT;
+        r.kind = reg ? OP_RFFT_REG : OP_RFFT;
         r.name = "rfft2";
         r.f = fp;
         r.bytes = px * 192 * 4 + pxs * 384 * 4;
@@ -678,7 +726,7 @@ struct Builder {
         gemm("fourier_conv", F.fu, {{spec, 1, false}}, {one_seg(0, 0, 384, SegSpec{0, 0, 384, 1, {{0, 0}}})}, 64, B, 1, h * wh,
              OutSpec{OUT_F32_NHWC, fu, 0, 384, 1, h * wh, 0, 0, nullptr}, 1, 0, 2.0 * pxs * 384 * 384);
         Op ir;
-        ir.kind = OP_IRFFT;
+        ir.kind = reg ? OP_IRFFT_REG : OP_IRFFT;
         ir.name = "irfft2";
         ir.f = fp;
         ir.bytes = pxs * 384 * 4 + px * 192 * 4 + px * 192 * 4;
@@ -755,12 +803,14 @@ struct Builder {
       gemm(names[u], e.W.ct[u], {{in, 1, true}}, cls, 64, B, in.H, in.W, split_out(outs[u]), 1, 0,
            2.0 * B * in.H * in.W * cout * in.C * 9);
     }
-    // OutConv 7x7 64 -> 3 over the reflect-pad-3 halo, + bias, sigmoid -> fp32 NCHW
+    // OutConv 7x7 64 -> 3 over the reflect-pad-3 halo, + bias, sigmoid -> fp32 NCHW:
+    // 7 row taps x 64 channels, N = (kx, co); 128-pixel row tiles stepping 122
+    // so every output's seven column partials sit in one tile
     {
-      ClassSpec c{0, 0, 3};
-      c.segs.push_back({0, 0, 64, 1, square_taps(7, 0)});
-      gemm("outconv_7x7", e.W.outc, {{U3, 1, false}}, {c}, 64, B, H, W,
-           OutSpec{OUT_F32_NCHW, out, 0, 3, H, W, 0, 0, nullptr}, 0, 1, 2.0 * B * H * W * 3 * 3136, 16);
+      std::vector<std::pair<int, int>> t;
+      for (int ky = 0; ky < 7; ky++) t.push_back({ky, 0});
+      gemm("outconv_7x7", e.W.outc, {{U3, 1, false}}, {one_seg(0, 0, 32, SegSpec{0, 0, 64, 1, t})}, 64, B, H, W,
+           OutSpec{OUT_SHIFT7_NCHW, out, 0, 3, H, W, 0, 0, nullptr}, 0, 1, 2.0 * B * H * W * 3 * 3136, 32, 122);
     }
   }
 };
@@ -870,7 +920,9 @@ template <class F>
 int guarded(lama_engine* e, F&& f) {
   if (!e) return LAMA_EINVAL;
   try {
+    if (!e->stream) throw EngineError{LAMA_EINVAL, "engine was not opened successfully"};
     CK(cudaSetDevice(e->device));
+    cudaGetLastError();  // a pending error from an earlier, unrelated call must not be reported here
     f();
     e->err.clear();
     return LAMA_OK;
@@ -905,7 +957,16 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
     e->err = "weights path is null";
     return LAMA_EINVAL;
   }
-  return guarded(e, [&] {
+  try {
+    WeightFile wf;
+    std::string err;
+    if (!wf.open(weights_path, err)) throw EngineError{LAMA_EWEIGHTS, err};
+    load_weights(wf, e->W);
+  } catch (const EngineError& x) {
+    e->err = x.msg;
+    return x.code;
+  }
+  try {
     int ndev = 0;
     CK(cudaGetDeviceCount(&ndev));
     if (device < 0 || device >= ndev)
@@ -922,12 +983,15 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     CKL(conv_gemm_prepare());
     CKL(fft_prepare(200 * 1024 + 4096));
+    CKL(fft_reg_prepare());
     e->d_err = (int*)e->wmem.alloc(256);
-    WeightFile wf;
-    std::string err;
-    if (!wf.open(weights_path, err)) throw EngineError{LAMA_EWEIGHTS, err};
-    load_weights(wf, e->wmem, e->W);
-  });
+    upload_weights(e->W, e->wmem);
+  } catch (const EngineError& x) {
+    e->err = x.msg;
+    return x.code;
+  }
+  e->err.clear();
+  return LAMA_OK;
 }
 
 int lama_forward(lama_engine* e, const float* in, int batch, int h, int w, float* out) {
@@ -1112,11 +1176,14 @@ int lama_debug_read(lama_engine* e, int batch, int h, int w, int op, float* out,
 
 void lama_close(lama_engine* e) {
   if (!e) return;
-  cudaSetDevice(e->device);
-  if (e->stream) cudaStreamSynchronize(e->stream);
+  if (e->stream) {
+    cudaSetDevice(e->device);
+    cudaStreamSynchronize(e->stream);
+  }
   e->plans.clear();
   e->wmem.free_all();
   if (e->stream) cudaStreamDestroy(e->stream);
+  cudaGetLastError();
   delete e;
 }
 

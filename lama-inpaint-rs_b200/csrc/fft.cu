@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(256) k_rfft2(const FftParams p) {
   float2* T = L + p.lmax;
   const int npairs = (p.h + 1) >> 1;
   const int sgn_w = direction(p.log2w, false), sgn_h = direction(p.log2h, false);
-  const float* in = p.feat;  // [B][h][w][C]
+  const float* in = p.feat;  // [B][C][h][w]
 
   // rows: two real rows per complex transform
   for (int item = warp; item < p.cg * npairs; item += kWarps) {
@@ -137,10 +137,10 @@ __global__ void __launch_bounds__(256) k_rfft2(const FftParams p) {
     const int c = c0 + cg;
     if (c >= p.c) continue;
     const int ya = 2 * yp, yb = 2 * yp + 1;
-    const float* ra = in + (((size_t)b * p.h + ya) * p.w) * p.c + c;
-    const float* rb = in + (((size_t)b * p.h + yb) * p.w) * p.c + c;
+    const float* ra = in + (((size_t)b * p.c + c) * p.h + ya) * p.w;
+    const float* rb = ra + p.w;
     for (int x = lane; x < p.w; x += 32)
-      L[x] = make_float2(ra[(size_t)x * p.c], yb < p.h ? rb[(size_t)x * p.c] : 0.f);
+      L[x] = make_float2(ra[x], yb < p.h ? rb[x] : 0.f);
     __syncwarp();
     warp_line_transform(L, T, s.tw_w, p.w, p.log2w, sgn_w);
     float2* za = s.Z + ((size_t)cg * p.h + ya) * p.wh;
@@ -236,13 +236,14 @@ __global__ void __launch_bounds__(256) k_irfft2(const FftParams p) {
     for (int x = lane; x < p.w; x += 32) {
       const float2 v = L[x];
       const size_t ia = (((size_t)b * p.h + ya) * p.w + x) * p.c + c;
-      const float va = v.x * p.scale + p.feat[ia];
+      const size_t fa = (((size_t)b * p.c + c) * p.h + ya) * p.w + x;
+      const float va = v.x * p.scale + p.feat[fa];
       const __nv_bfloat16 ha = __float2bfloat16_rn(va);
       out[ia] = ha;
       out[p.s_part + ia] = __float2bfloat16_rn(va - __bfloat162float(ha));
       if (yb < p.h) {
         const size_t ib = ia + (size_t)p.w * p.c;
-        const float vb = v.y * p.scale + p.feat[ib];
+        const float vb = v.y * p.scale + p.feat[fa + p.w];
         const __nv_bfloat16 hb = __float2bfloat16_rn(vb);
         out[ib] = hb;
         out[p.s_part + ib] = __float2bfloat16_rn(vb - __bfloat162float(hb));

@@ -16,7 +16,7 @@ struct FftParams {
   float scale;             // 1/sqrt(h*w)
   const float2* tw_h;      // (cos, sin)(2 pi k / h), k < h
   const float2* tw_w;      // (cos, sin)(2 pi k / w), k < w
-  const float* feat;       // [B][h][w][c] fp32: rfft2 input / irfft2 residual
+  const float* feat;       // [B][c][h][w] fp32 (NCHW): rfft2 input / irfft2 residual
   void* spec;              // rfft2 out: split bf16 [2][B][h][wh][2c]
   long long spec_part;
   const float* fu;         // irfft2 in: fp32 [B][h][wh][2c]
@@ -28,5 +28,11 @@ size_t fft_smem_bytes(const FftParams& p);
 int fft_prepare(size_t max_smem);
 int launch_rfft2(const FftParams& p, cudaStream_t st);
 int launch_irfft2(const FftParams& p, cudaStream_t st);
+
+// Register-resident kernels for power-of-two planes with sides in {8..64}
+// (fft_reg.cu).
+bool fft_reg_supported(int h, int w);
+int fft_reg_prepare();
+int launch_fft_reg(const FftParams& p, bool inverse, cudaStream_t st);
 
 }  // namespace lama

@@ -1,0 +1,321 @@
+// Register-resident rfft2 / irfft2 for power-of-two planes up to 64 x 64.
+//
+// Same semantics as fft.cu (the reference's rfft2_ortho / irfft2_ortho,
+// lama-rs/src/cpu.rs:769-837; power-of-two lengths use the standard transform
+// directions there, cpu.rs:888-927), organised for throughput:
+//   * one CTA = one image x 8 channels, 256 threads; thread t works on
+//     channel t % 8, so a warp covers 8 channels x 4 lines and every global
+//     access moves whole 16-64 byte channel groups;
+//   * every 1-D transform lives in one thread's registers (fully unrolled
+//     radix-2, twiddles from constant memory);
+//   * rows: a real length-W row is one complex length-W/2 transform plus the
+//     even/odd untangling (the half-length real-FFT identity);
+//   * columns: after the row pass the DC and Nyquist columns are real, so
+//     they share one complex transform, and each channel needs exactly W/2
+//     column transforms; the inverse packs the Hermitian parts of those two
+//     columns the same way (the row c2r ignores their imaginary parts);
+//   * the plane sits in shared memory as [c][kx][y] with strides padded so
+//     that both the row-thread and the column-thread access patterns are
+//     bank-conflict free.
+// Input feat is fp32 NCHW (written so by the conv1 epilogue); the spectrum
+// and S are split bf16 NHWC operands of the following GEMMs.
+#include <cstdint>
+
+#include "fft.cuh"
+#include "ptx.cuh"
+
+namespace lama {
+
+__constant__ float2 c_tw64[64];  // (cos, sin)(2 pi m / 64)
+
+namespace {
+
+constexpr int CG = 8;        // channels per CTA
+constexpr int YS = 65;       // smem y stride (float2) of one column
+constexpr int KS = 34;       // smem kx slots per channel (>= 33, stride = 4 words mod 32)
+
+__host__ __device__ constexpr int ilog2(int n) { return n <= 1 ? 0 : 1 + ilog2(n >> 1); }
+__host__ __device__ constexpr int brev(int i, int bits) {
+  int r = 0;
+  for (int b = 0; b < bits; b++) r |= ((i >> b) & 1) << (bits - 1 - b);
+  return r;
+}
+
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 conjf2(float2 a) { return make_float2(a.x, -a.y); }
+
+// e^{sign * 2 pi i m / n} for n | 64
+template <int N, bool INV>
+__device__ __forceinline__ float2 twid(int m) {
+  float2 w = c_tw64[(m * (64 / N)) & 63];
+  if (!INV) w.y = -w.y;
+  return w;
+}
+
+// One radix-2 stage of span LEN, then the next.
+template <int N, bool INV, int LEN>
+__device__ __forceinline__ void fft_stages(float2 (&a)[N]) {
+  if constexpr (LEN <= N) {
+#pragma unroll
+    for (int i = 0; i < N; i += LEN) {
+#pragma unroll
+      for (int k = 0; k < LEN / 2; k++) {
+        const float2 u = a[i + k];
+        float2 v = a[i + k + LEN / 2];
+        if (k != 0) v = cmul(v, twid<LEN, INV>(k));
+        a[i + k] = cadd(u, v);
+        a[i + k + LEN / 2] = csub(u, v);
+      }
+    }
+    fft_stages<N, INV, LEN * 2>(a);
+  }
+}
+
+// Unnormalised in-register DFT of length N (power of two <= 64).
+// INV = false: sum x_j e^{-2 pi i jk/N};  INV = true: e^{+...}.
+template <int N, bool INV>
+__device__ __forceinline__ void fft_reg(float2 (&a)[N]) {
+  constexpr int B = ilog2(N);
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    const int j = brev(i, B);
+    if (i < j) {
+      float2 t = a[i];
+      a[i] = a[j];
+      a[j] = t;
+    }
+  }
+  fft_stages<N, INV, 2>(a);
+}
+
+struct Layout {
+  float2* Z;  // [CG][KS][YS]
+  __device__ __forceinline__ float2& at(int c, int kx, int y) const { return Z[(c * KS + kx) * YS + y]; }
+};
+
+// ------------------------------------------------------------------ rfft2
+template <int H, int W>
+__global__ void __launch_bounds__(256) k_rfft2_reg(const FftParams p) {
+  constexpr int WH = W / 2 + 1, HALF = W / 2;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const Layout L{reinterpret_cast<float2*>(smem_raw)};
+  const int t = threadIdx.x, c = t % CG, q = t / CG;
+  const int b = blockIdx.y, cc = blockIdx.x * CG + c;
+  const bool live = cc < p.c;
+
+  // rows: x real, length W -> bins 0..W/2 via one complex length-W/2 transform
+#pragma unroll 1
+  for (int y = q; y < H; y += 32) {
+    if (live) {
+      const float4* row = reinterpret_cast<const float4*>(p.feat + (((size_t)b * p.c + cc) * H + y) * W);
+      float2 z[HALF];
+#pragma unroll
+      for (int i = 0; i < W / 4; i++) {
+        const float4 v = __ldg(row + i);
+        z[2 * i] = make_float2(v.x, v.y);
+        z[2 * i + 1] = make_float2(v.z, v.w);
+      }
+      fft_reg<HALF, false>(z);
+#pragma unroll
+      for (int k = 0; k <= HALF; k++) {
+        const float2 zk = z[k % HALF], zm = conjf2(z[(HALF - k) % HALF]);
+        const float2 e = make_float2(0.5f * (zk.x + zm.x), 0.5f * (zk.y + zm.y));  // even-sample DFT
+        const float2 d = make_float2(0.5f * (zk.x - zm.x), 0.5f * (zk.y - zm.y));
+        const float2 o = make_float2(d.y, -d.x);                                    // odd-sample DFT = d / i
+        L.at(c, k, y) = cadd(e, cmul(o, twid<W, false>(k)));
+      }
+    }
+  }
+  __syncthreads();
+
+  // columns: slot 0 packs the (real) DC and Nyquist columns, slots 1..W/2-1 are kx
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.spec);
+  const int C2 = 2 * p.c;
+  if (live && q < HALF) {
+    float2 a[H];
+    if (q == 0) {
+#pragma unroll
+      for (int y = 0; y < H; y++) a[y] = make_float2(L.at(c, 0, y).x, L.at(c, HALF, y).x);
+    } else {
+#pragma unroll
+      for (int y = 0; y < H; y++) a[y] = L.at(c, q, y);
+    }
+    fft_reg<H, false>(a);
+    auto store = [&](int ky, int kx, float2 v) {
+      uint32_t hi, lo;
+      split_pair(v.x * p.scale, v.y * p.scale, hi, lo);
+      const size_t off = (((size_t)b * H + ky) * WH + kx) * C2 + 2 * cc;
+      *reinterpret_cast<uint32_t*>(out + off) = hi;
+      *reinterpret_cast<uint32_t*>(out + p.spec_part + off) = lo;
+    };
+    if (q == 0) {
+#pragma unroll
+      for (int ky = 0; ky < H; ky++) {
+        const float2 zk = a[ky], zm = conjf2(a[(H - ky) % H]);
+        store(ky, 0, make_float2(0.5f * (zk.x + zm.x), 0.5f * (zk.y + zm.y)));
+        const float2 d = make_float2(0.5f * (zk.x - zm.x), 0.5f * (zk.y - zm.y));
+        store(ky, HALF, make_float2(d.y, -d.x));
+      }
+    } else {
+#pragma unroll
+      for (int ky = 0; ky < H; ky++) store(ky, q, a[ky]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ irfft2 (+ feat)
+template <int H, int W>
+__global__ void __launch_bounds__(256) k_irfft2_reg(const FftParams p) {
+  constexpr int WH = W / 2 + 1, HALF = W / 2;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const Layout L{reinterpret_cast<float2*>(smem_raw)};
+  const int t = threadIdx.x, c = t % CG, q = t / CG;
+  const int b = blockIdx.y, cc = blockIdx.x * CG + c;
+  const bool live = cc < p.c;
+  const int C2 = 2 * p.c;
+
+  // columns (inverse): slot 0 transforms the Hermitian parts of the DC and
+  // Nyquist columns together (only their real outputs are used)
+  if (live && q < HALF) {
+    float2 a[H];
+    auto ld = [&](int ky, int kx) {
+      const float2* s = reinterpret_cast<const float2*>(p.fu + (((size_t)b * H + ky) * WH + kx) * C2 + 2 * cc);
+      return __ldg(s);
+    };
+    if (q == 0) {
+#pragma unroll
+      for (int k = 0; k <= H / 2; k++) {
+        const int km = (H - k) % H;
+        const float2 a0 = ld(k, 0), a0m = ld(km, 0), an = ld(k, HALF), anm = ld(km, HALF);
+        // Hermitian parts h(k) = (v(k) + conj(v(-k))) / 2; z = h0 + i*hn
+        const float2 h0 = make_float2(0.5f * (a0.x + a0m.x), 0.5f * (a0.y - a0m.y));
+        const float2 hn = make_float2(0.5f * (an.x + anm.x), 0.5f * (an.y - anm.y));
+        a[k] = make_float2(h0.x - hn.y, h0.y + hn.x);
+        // h(-k) = conj(h(k))
+        a[km] = make_float2(h0.x + hn.y, -h0.y + hn.x);
+      }
+    } else {
+#pragma unroll
+      for (int ky = 0; ky < H; ky++) a[ky] = ld(ky, q);
+    }
+    fft_reg<H, true>(a);
+    if (q == 0) {
+#pragma unroll
+      for (int y = 0; y < H; y++) {
+        L.at(c, 0, y) = make_float2(a[y].x, 0.f);
+        L.at(c, HALF, y) = make_float2(a[y].y, 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int y = 0; y < H; y++) L.at(c, q, y) = a[y];
+    }
+  }
+  __syncthreads();
+
+  // rows: Hermitian completion + real inverse via one complex length-W/2 transform
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.s_out);
+#pragma unroll 1
+  for (int y = q; y < H; y += 32) {
+    if (!live) continue;
+    float2 z[HALF];
+#pragma unroll
+    for (int k = 0; k < HALF; k++) {
+      const float2 xk = L.at(c, k, y);
+      const float2 xm = conjf2(L.at(c, HALF - k, y));
+      const float2 e = cadd(xk, xm);                               // X[k] + X[k+W/2]
+      const float2 o = cmul(csub(xk, xm), twid<W, true>(k));       // (X[k] - X[k+W/2]) e^{+2 pi i k/W}
+      z[k] = make_float2(e.x - o.y, e.y + o.x);                    // e + i*o
+    }
+    fft_reg<HALF, true>(z);
+    const float4* fr = reinterpret_cast<const float4*>(p.feat + (((size_t)b * p.c + cc) * H + y) * W);
+    __nv_bfloat16* o = out + ((size_t)b * H + y) * W * p.c + cc;
+#pragma unroll
+    for (int i = 0; i < W / 4; i++) {
+      const float4 f = __ldg(fr + i);
+      const float v[4] = {z[2 * i].x * p.scale + f.x, z[2 * i].y * p.scale + f.y,
+                          z[2 * i + 1].x * p.scale + f.z, z[2 * i + 1].y * p.scale + f.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+        const size_t off = (size_t)(4 * i + j) * p.c;
+        o[off] = h;
+        o[p.s_part + off] = __float2bfloat16_rn(v[j] - __bfloat162float(h));
+      }
+    }
+  }
+}
+
+template <int H, int W>
+int launch_pair(const FftParams& p, bool inverse, cudaStream_t st) {
+  const size_t smem = (size_t)CG * KS * YS * sizeof(float2);
+  dim3 grid((p.c + CG - 1) / CG, p.batch);
+  if (inverse) k_irfft2_reg<H, W><<<grid, 256, smem, st>>>(p);
+  else k_rfft2_reg<H, W><<<grid, 256, smem, st>>>(p);
+  return (int)cudaGetLastError();
+}
+
+template <int H, int W>
+int prepare_pair() {
+  const int smem = (int)((size_t)CG * KS * YS * sizeof(float2));
+  cudaError_t e = cudaFuncSetAttribute(k_rfft2_reg<H, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return (int)e;
+  return (int)cudaFuncSetAttribute(k_irfft2_reg<H, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
+template <int H>
+int dispatch_w(const FftParams& p, bool inv, cudaStream_t st) {
+  switch (p.w) {
+    case 8: return launch_pair<H, 8>(p, inv, st);
+    case 16: return launch_pair<H, 16>(p, inv, st);
+    case 32: return launch_pair<H, 32>(p, inv, st);
+    case 64: return launch_pair<H, 64>(p, inv, st);
+  }
+  return -1;
+}
+
+template <int H>
+int prepare_w() {
+  int e;
+  if ((e = prepare_pair<H, 8>())) return e;
+  if ((e = prepare_pair<H, 16>())) return e;
+  if ((e = prepare_pair<H, 32>())) return e;
+  return prepare_pair<H, 64>();
+}
+
+}  // namespace
+
+bool fft_reg_supported(int h, int w) {
+  auto ok = [](int n) { return n == 8 || n == 16 || n == 32 || n == 64; };
+  return ok(h) && ok(w);
+}
+
+int fft_reg_prepare() {
+  float2 tw[64];
+  for (int m = 0; m < 64; m++) {
+    const double a = 2.0 * 3.14159265358979323846 * (double)m / 64.0;
+    tw[m] = make_float2((float)cos(a), (float)sin(a));
+  }
+  cudaError_t e = cudaMemcpyToSymbol(c_tw64, tw, sizeof(tw));
+  if (e != cudaSuccess) return (int)e;
+  int r;
+  if ((r = prepare_w<8>())) return r;
+  if ((r = prepare_w<16>())) return r;
+  if ((r = prepare_w<32>())) return r;
+  return prepare_w<64>();
+}
+
+int launch_fft_reg(const FftParams& p, bool inverse, cudaStream_t st) {
+  switch (p.h) {
+    case 8: return dispatch_w<8>(p, inverse, st);
+    case 16: return dispatch_w<16>(p, inverse, st);
+    case 32: return dispatch_w<32>(p, inverse, st);
+    case 64: return dispatch_w<64>(p, inverse, st);
+  }
+  return -1;
+}
+
+}  // namespace lama

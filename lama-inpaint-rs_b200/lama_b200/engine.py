@@ -209,6 +209,16 @@ class Engine:
         b, _, h, w = x.shape
         self._check(lib().lama_debug_run(self._h, _fp(x), b, h, w, n_ops))
 
+    def op_names(self, batch: int, h: int, w: int):
+        """Launch names of the f32 forward plan at this shape, in order."""
+        names = []
+        for i in range(self.launch_count(batch, h, w)):
+            dims = (ctypes.c_int * 4)()
+            name = ctypes.create_string_buffer(32)
+            self._check(lib().lama_debug_read(self._h, batch, h, w, i, None, 0, dims, name))
+            names.append(name.value.decode())
+        return names
+
     def debug_read(self, batch: int, h: int, w: int, op: int):
         dims = (ctypes.c_int * 4)()
         name = ctypes.create_string_buffer(32)

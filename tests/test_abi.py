@@ -1,0 +1,43 @@
+"""The C-ABI library loads and exports every symbol include/lama_b200.h declares.
+
+No compute calls: this runs on a machine without a GPU.
+"""
+
+import ctypes
+import os
+import re
+
+from lama_b200 import engine
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "lama_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(lama_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_the_operator_surface():
+    names = declared_functions()
+    for n in ("lama_open", "lama_forward", "lama_inpaint_u8", "lama_last_error", "lama_close"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(engine.LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_every_declared_symbol():
+    bound = {n for n, _, _ in engine.SIGNATURES}
+    assert set(declared_functions()) <= bound
+
+
+def test_abi_version_is_callable_without_a_gpu():
+    assert engine.lib().lama_abi_version() == 1
+
+
+def test_last_error_on_null_engine():
+    assert engine.lib().lama_last_error(None) == b"null engine"

@@ -1,0 +1,186 @@
+"""Parity of the B200 engine with the CPU oracle (a restatement of lama-rs/src/cpu.rs).
+
+Tolerances (the reference is FP32; the engine computes convolutions as three
+BF16 products of split operands with FP32 accumulation):
+  * sigmoid output (pre-quantisation float): max |diff| <= 1e-4;
+  * intermediate activations: max |diff| <= 1e-4 x max |expected| per layer,
+    and <= 2e-3 x max |expected| after the 18-block stack with the BASELINE
+    init, whose activations grow to ~1e10;
+  * u8 composite: <= 1 level per pixel, mean <= 0.1 levels over masked
+    pixels, unmasked pixels bit-exact (lama-rs/src/main.rs:272-307).
+"""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import make_input
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+FLOAT_TOL = 1e-4
+
+
+def _interior(a, halo):
+    if halo:
+        a = a[:, halo:-halo, halo:-halo, :]
+    return a.transpose(0, 3, 1, 2)
+
+
+def test_encoder_and_first_block_layer_by_layer(engine_tamed):
+    """Every launch of the encoder and of resblock model.5 against float64 torch."""
+    from lama_b200 import plan, seeded
+    from torch_ref import TorchRef, irfft2_ortho, rfft2_ortho
+    h = w = 64
+    _, _, x = make_input(h, w, 11)
+    ref = TorchRef(dict(seeded.make_weights(res_scale=seeded.TAMED_RES_SCALE)))
+    xt = F.pad(torch.from_numpy(x).double()[None], (3, 3, 3, 3), mode="reflect")
+    exp = []
+    xl, xg = xt, None
+    with torch.no_grad():
+        for b in plan.encoder():
+            xl, xg = ref.ffc(b, xl, xg)
+            exp.append(xl if xg is None else torch.cat([xl, xg], 1))
+        XA = exp[-1]
+        b1, b2 = plan.resblocks()[0]
+        p = b1.ffc_prefix + ".convg2g"
+        xl, xg = XA[:, :128], XA[:, 128:]
+        feat = ref.bn(F.conv2d(xg, ref.t[p + ".conv1.0.weight"]), p + ".conv1.1")
+        sp = rfft2_ortho(feat)
+        st = torch.stack((sp.real, sp.imag), -1).permute(0, 1, 4, 2, 3).reshape(1, 384, 8, 5)
+        fu = ref.bn(F.conv2d(st, ref.t[p + ".fu.conv_layer.weight"]), p + ".fu.bn")
+        y = fu.reshape(1, 192, 2, 8, 5).permute(0, 1, 3, 4, 2)
+        S = feat + irfft2_ortho(torch.complex(y[..., 0].contiguous(), y[..., 1].contiguous()), 8, 8)
+        l1, g1 = ref.ffc(b1, xl, xg)
+        l2, g2 = ref.ffc(b2, l1, g1)
+    expected = {
+        1: exp[0].numpy(), 2: exp[1].numpy(), 3: exp[2].numpy(), 4: exp[3].numpy(),
+        5: feat.numpy(), 6: st.numpy().transpose(0, 2, 3, 1),
+        7: fu.numpy().transpose(0, 2, 3, 1).reshape(1, 1, 40, 384), 8: S.numpy().transpose(0, 2, 3, 1),
+        9: torch.cat([l1, g1], 1).numpy(), 14: torch.cat([xl + l2, xg + g2], 1).numpy(),
+    }
+    names = {1: "model1_7x7", 2: "model2_3x3s2", 3: "model3_3x3s2", 4: "model4_3x3s2", 5: "spectral_conv1",
+             6: "rfft2", 7: "fourier_conv", 8: "irfft2", 9: "ffc_out", 14: "ffc_out"}
+    for op, e in expected.items():
+        engine_tamed.debug_run(x, op + 1)
+        name, got = engine_tamed.debug_read(1, h, w, op)
+        assert name == names[op]
+        if op in (1, 2, 3, 4, 9, 14):
+            got = _interior(got, 1)
+        got = got.reshape(e.shape)
+        err = np.abs(got - e).max() / np.abs(e).max()
+        assert err < 1e-4, (name, err)
+
+
+@pytest.mark.parametrize("h,w,seed", [(64, 64, 1), (72, 56, 2), (128, 128, 3), (48, 80, 4), (8, 8, 5), (24, 40, 6)])
+def test_forward_matches_oracle(engine_tamed, oracle_tamed, h, w, seed):
+    """Includes non-power-of-two latents (9x7, 6x10, 3x5: the reference's
+    opposite-direction Bluestein transforms) and the 1x1 latent of an 8x8 input."""
+    _, _, x = make_input(h, w, seed)
+    got = engine_tamed.forward(x)
+    exp = oracle_tamed.forward(x)
+    assert np.abs(got - exp).max() <= FLOAT_TOL
+
+
+def test_batch_equals_single_images(engine_tamed):
+    xs = np.stack([make_input(64, 64, s)[2] for s in (21, 22, 23)])
+    batch = engine_tamed.forward(xs)
+    for i in range(3):
+        np.testing.assert_array_equal(batch[i], engine_tamed.forward(xs[i]))
+
+
+def test_forward_is_deterministic(engine_tamed):
+    _, _, x = make_input(64, 64, 7)
+    np.testing.assert_array_equal(engine_tamed.forward(x), engine_tamed.forward(x))
+
+
+@pytest.mark.parametrize("h,w,seed", [(64, 64, 31), (61, 77, 32), (96, 40, 33)])
+def test_inpaint_u8_matches_oracle_composite(engine_tamed, oracle_tamed, h, w, seed):
+    img, m, x = make_input(h, w, seed)
+    got = engine_tamed.inpaint_u8(img, m)
+    exp = O.composite(img, m, oracle_tamed.forward(x))
+    d = np.abs(got.astype(int) - exp.astype(int))
+    assert d.max() <= 1
+    assert d[m > 0].mean() <= 0.1
+    np.testing.assert_array_equal(got[m == 0], img[m == 0])
+
+
+def test_inpaint_u8_empty_and_full_masks(engine_tamed, oracle_tamed):
+    img, _, _ = make_input(32, 32, 41)
+    empty = np.zeros((32, 32), np.uint8)
+    np.testing.assert_array_equal(engine_tamed.inpaint_u8(img, empty), img)
+    full = np.full((32, 32), 255, np.uint8)
+    got = engine_tamed.inpaint_u8(img, full)
+    exp = O.composite(img, full, oracle_tamed.forward(O.build_input(img, full, 0, 0)))
+    assert np.abs(got.astype(int) - exp.astype(int)).max() <= 1
+
+
+def test_resblock_stack_with_baseline_init(engine_baseline, oracle_baseline):
+    """Config 1 (the 18-block stack) with the BASELINE init, whose activations
+    grow ~3.5x per block: relative error stays bounded."""
+    rng = np.random.default_rng(5)
+    l = rng.standard_normal((128, 16, 16)).astype(np.float32)
+    g = rng.standard_normal((384, 16, 16)).astype(np.float32)
+    gl, gg = engine_baseline.resblocks(l, g, 18)
+    el, eg = oracle_baseline.resblocks(l, g, 18)
+    scale = max(np.abs(el).max(), np.abs(eg).max())
+    assert scale > 1e6
+    assert np.abs(gl - el).max() / scale < 2e-3
+    assert np.abs(gg - eg).max() / scale < 2e-3
+
+
+def test_resblock_stack_tamed_and_partial_depth(engine_tamed, oracle_tamed):
+    rng = np.random.default_rng(6)
+    l = rng.standard_normal((128, 8, 8)).astype(np.float32)
+    g = rng.standard_normal((384, 8, 8)).astype(np.float32)
+    for nb in (0, 1, 18):
+        gl, gg = engine_tamed.resblocks(l, g, nb)
+        el, eg = oracle_tamed.resblocks(l, g, nb)
+        scale = max(np.abs(el).max(), np.abs(eg).max())
+        assert np.abs(gl - el).max() / scale < 1e-4, nb
+        assert np.abs(gg - eg).max() / scale < 1e-4, nb
+
+
+def test_baseline_init_full_pass(engine_baseline, oracle_baseline):
+    """With the BASELINE init the sigmoid saturates; the saturated output and
+    the last resblock's activations (~1e10) still match."""
+    _, _, x = make_input(64, 64, 8)
+    got = engine_baseline.forward(x)
+    exp = oracle_baseline.forward(x)
+    assert np.abs(got - exp).max() <= FLOAT_TOL
+    names = engine_baseline.op_names(1, 64, 64)
+    last = max(i for i, n in enumerate(names) if n == "ffc_out")
+    engine_baseline.debug_run(x, last + 1)
+    _, got_x = engine_baseline.debug_read(1, 64, 64, last)
+    dump = oracle_baseline.forward_dump(x, 22)
+    exp_x = np.concatenate([dump[: 128 * 64].reshape(128, 8, 8), dump[128 * 64:].reshape(384, 8, 8)])
+    got_x = _interior(got_x, 1)[0]
+    assert np.abs(got_x - exp_x).max() / np.abs(exp_x).max() < 2e-3
+
+
+def test_invalid_sizes_are_errors(engine_tamed):
+    from lama_b200 import LamaError
+    with pytest.raises(LamaError) as ei:
+        engine_tamed.forward(np.zeros((4, 60, 64), np.float32))
+    assert ei.value.code == -1 and "multiples of 8" in ei.value.msg
+
+
+def test_bad_device_is_an_error(weights_tamed):
+    from lama_b200 import Engine, LamaError
+    with pytest.raises(LamaError) as ei:
+        Engine(weights_tamed, 4096)
+    assert ei.value.code == -1
+
+
+def test_full_size_512_batch_properties(engine_baseline):
+    """Config 0 geometry at full size: finite, in [0,1], deterministic, and
+    identical inputs in a batch give identical outputs."""
+    _, _, x = make_input(512, 512, 0)
+    xs = np.stack([x, x])
+    a = engine_baseline.forward(xs)
+    assert np.isfinite(a).all() and a.min() >= 0 and a.max() <= 1
+    np.testing.assert_array_equal(a[0], a[1])
+    np.testing.assert_array_equal(a, engine_baseline.forward(xs))
