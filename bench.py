@@ -185,6 +185,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout (one JSON line)
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
@@ -199,7 +200,8 @@ def main():
     eng = Engine(wpath, local)
     stream = torch.cuda.ExternalStream(eng.stream())
 
-    mine = list(range(rank, TOTAL_IMAGES, world))
+    from lama_b200.replicas import chunks as make_chunks, max_over_ranks, shard
+    mine = shard(TOTAL_IMAGES, rank, world)
     n = len(mine)
     rgb_d, mask_d = make_data(N_DISTINCT, SIZE)
     idx = np.array([i % N_DISTINCT for i in mine])
@@ -209,7 +211,7 @@ def main():
     rgb = rgb_h.cuda()
     mask = mask_h.cuda()
     out = torch.empty_like(rgb)
-    chunks = [(s, min(args.chunk, n - s)) for s in range(0, n, args.chunk)]
+    chunks = make_chunks(n, args.chunk)
     px = SIZE * SIZE
 
     def step_device():
@@ -237,11 +239,7 @@ def main():
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
         barrier()
-        if world > 1:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = t.item()
-        return ms
+        return max_over_ranks(ms, world, device="cuda")
 
     for _ in range(args.warmup):
         step_device()

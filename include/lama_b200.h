@@ -124,10 +124,30 @@ int lama_profile_forward(lama_engine* e, const float* d_in, int batch, int h, in
  * pairs are summed); dims receives (batch, rows, cols, channels) of the
  * stored NHWC layout including any halo, or (batch, C, H, W) for NCHW
  * outputs; name receives the launch name (32 bytes).  With out == NULL only
- * dims and name are filled.  Returns the launch count through the plan. */
+ * dims and name are filled. */
 int lama_debug_run(lama_engine* e, const float* in, int batch, int h, int w, int n_ops);
 int lama_debug_read(lama_engine* e, int batch, int h, int w, int op, float* out, long long cap, int* dims,
                     char* name);
+
+/* Host helpers of the CLI's --tile / --sections modes (no GPU needed).
+ * They restate lama-rs/src/main.rs's geometry with the same constants
+ * (window >= 512, sections of 256, multiples of 8) and ordering. */
+
+/* Top-left of a `side`-long window centred on c, kept inside [0, extent-side]
+ * (main.rs:722-727). */
+int lama_window_origin(int c, int side, int extent);
+
+/* The --tile window of a w x h mask (non-zero = hole): out = {x0, y0, side,
+ * bbox_w, bbox_h}.  Returns 1, or 0 for an empty mask (main.rs:740-777). */
+int lama_tile_rect(const uint8_t* mask, int w, int h, int* out);
+
+/* Distance of every masked pixel to the rim of the hole (4-neighbour BFS);
+ * UINT32_MAX for unmasked pixels (main.rs:664-717). */
+int lama_mask_depth(const uint8_t* mask, int w, int h, uint32_t* depth);
+
+/* The --sections pieces, rim first: up to `cap` rectangles {x0, y0, x1, y1}
+ * (exclusive ends) written to `out`; returns their count (main.rs:597-659). */
+int lama_section_rects(const uint8_t* mask, int w, int h, int* out, int cap);
 
 /* Free every device buffer and the engine. */
 void lama_close(lama_engine* e);

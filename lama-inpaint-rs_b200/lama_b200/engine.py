@@ -66,8 +66,14 @@ SIGNATURES = [
     ("lama_debug_run", ctypes.c_int, [_vp, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     ("lama_debug_read", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p,
                                        ctypes.c_longlong, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p]),
+    ("lama_window_origin", ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    ("lama_tile_rect", ctypes.c_int, [_u8p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    ("lama_mask_depth", ctypes.c_int, [_u8p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
+    ("lama_section_rects", ctypes.c_int, [_u8p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                          ctypes.c_int]),
     ("lama_close", None, [_vp]),
 ]
+CLI_PATH = os.path.join(PKG_ROOT, "lama-inpaint")
 
 
 def lib():
@@ -92,6 +98,36 @@ def _fp(a):
 
 def _up(a):
     return a.ctypes.data_as(_u8p)
+
+
+# ------------------------------------------------------------ host geometry (no GPU)
+
+def window_origin(c: int, side: int, extent: int) -> int:
+    return lib().lama_window_origin(c, side, extent)
+
+
+def tile_rect(mask: np.ndarray):
+    """--tile window (x0, y0, side, bbox_w, bbox_h) or None for an empty mask."""
+    m = np.ascontiguousarray(mask, np.uint8)
+    out = (ctypes.c_int * 5)()
+    r = lib().lama_tile_rect(_up(m), m.shape[1], m.shape[0], out)
+    return tuple(out) if r == 1 else None
+
+
+def mask_depth(mask: np.ndarray) -> np.ndarray:
+    m = np.ascontiguousarray(mask, np.uint8)
+    d = np.empty(m.shape, np.uint32)
+    lib().lama_mask_depth(_up(m), m.shape[1], m.shape[0], d.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+    return d
+
+
+def section_rects(mask: np.ndarray):
+    """--sections pieces [(x0, y0, x1, y1)], rim first."""
+    m = np.ascontiguousarray(mask, np.uint8)
+    n = lib().lama_section_rects(_up(m), m.shape[1], m.shape[0], None, 0)
+    out = (ctypes.c_int * (4 * max(n, 1)))()
+    lib().lama_section_rects(_up(m), m.shape[1], m.shape[0], out, n)
+    return [tuple(out[4 * i: 4 * i + 4]) for i in range(n)]
 
 
 class Engine:

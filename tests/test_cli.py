@@ -1,0 +1,96 @@
+"""The C++ CLI (lama-inpaint-rs_b200/lama-inpaint): argument contract and PNG codec.
+
+Usage errors exit 2 and run errors exit 1 (lama-rs/src/main.rs:198-210); the
+PNG reader accepts what the reference's reader accepts (lama-rs/src/image.rs:80-130),
+checked against PIL.  End-to-end inpainting through the CLI is a GPU test.
+"""
+
+import os
+import subprocess
+
+import numpy as np
+import pytest
+from PIL import Image
+
+from lama_b200.engine import CLI_PATH
+
+pytestmark = pytest.mark.skipif(not os.path.exists(CLI_PATH), reason="CLI not built")
+
+
+def run(*args, **kw):
+    return subprocess.run([CLI_PATH, *args], capture_output=True, text=True, **kw)
+
+
+def test_help_exits_zero():
+    r = run("--help")
+    assert r.returncode == 0 and "--tile" in r.stdout and "--sections" in r.stdout
+
+
+@pytest.mark.parametrize("args,msg", [
+    ([], "--image is required"),
+    (["--image", "a.png"], "--mask is required"),
+    (["--image", "a.png", "--mask", "b.png"], "--output is required"),
+    (["--image", "-", "--mask", "-", "--output", "o.png"], "cannot both be '-'"),
+    (["--image", "a", "--mask", "b", "--output", "o", "--tile", "--sections"], "mutually exclusive"),
+    (["--bogus"], "unknown argument --bogus"),
+    (["--image"], "--image needs a value"),
+])
+def test_usage_errors_exit_2(args, msg):
+    r = run(*args)
+    assert r.returncode == 2 and msg in r.stderr
+
+
+def test_size_mismatch_is_a_run_error(tmp_path):
+    Image.fromarray(np.zeros((8, 8, 3), np.uint8)).save(tmp_path / "a.png")
+    Image.fromarray(np.zeros((8, 9), np.uint8)).save(tmp_path / "m.png")
+    r = run("--image", str(tmp_path / "a.png"), "--mask", str(tmp_path / "m.png"), "--output", str(tmp_path / "o.png"))
+    assert r.returncode == 1 and "mask is 9x8 but image is 8x8" in r.stderr
+
+
+def test_cpu_flag_is_refused(tmp_path):
+    Image.fromarray(np.zeros((8, 8, 3), np.uint8)).save(tmp_path / "a.png")
+    Image.fromarray(np.zeros((8, 8), np.uint8)).save(tmp_path / "m.png")
+    r = run("--image", str(tmp_path / "a.png"), "--mask", str(tmp_path / "m.png"), "--output",
+            str(tmp_path / "o.png"), "--cpu")
+    assert r.returncode == 1 and "no CPU engine" in r.stderr
+
+
+def _rgb_expected(im: Image.Image) -> np.ndarray:
+    """What image.rs:80-120 produces: RGB8 (16-bit high byte, alpha dropped)."""
+    if im.mode == "P":
+        return np.asarray(im.convert("RGB"))
+    if im.mode in ("I;16", "I;16B", "I"):
+        a = np.asarray(im).astype(np.uint32) >> 8
+        return np.repeat(a.astype(np.uint8)[..., None], 3, axis=2)
+    return np.asarray(im.convert("RGB"))
+
+
+@pytest.mark.parametrize("mode", ["RGB", "RGBA", "L", "LA", "P", "I;16"])
+@pytest.mark.parametrize("interlace", [False, True])
+def test_png_decode_matches_pil(tmp_path, mode, interlace):
+    rng = np.random.default_rng(3)
+    h, w = 37, 53
+    if mode == "I;16":
+        im = Image.fromarray(rng.integers(0, 65535, (h, w), dtype=np.uint16))
+    else:
+        im = Image.fromarray(rng.integers(0, 255, (h, w, 3), dtype=np.uint8)).convert(mode)
+    src = tmp_path / "in.png"
+    im.save(src, interlace=interlace) if not interlace else im.save(src, optimize=False, interlace=1)
+    dst = tmp_path / "out.png"
+    r = run("--decode-png", str(src), str(dst))
+    assert r.returncode == 0, r.stderr
+    got = np.asarray(Image.open(dst))
+    np.testing.assert_array_equal(got, _rgb_expected(Image.open(src)))
+
+
+def test_png_rejects_garbage(tmp_path):
+    p = tmp_path / "bad.png"
+    p.write_bytes(b"not a png at all")
+    r = run("--decode-png", str(p), str(tmp_path / "o.png"))
+    assert r.returncode == 1 and "not a PNG" in r.stderr
+
+
+def test_png_rejects_low_bit_depth(tmp_path):
+    Image.fromarray(np.zeros((4, 4), bool)).save(tmp_path / "b.png")  # 1-bit
+    r = run("--decode-png", str(tmp_path / "b.png"), str(tmp_path / "o.png"))
+    assert r.returncode == 1 and "bit depth" in r.stderr
