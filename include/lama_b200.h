@@ -90,6 +90,14 @@ int lama_resblocks(lama_engine* e, const float* local_in, const float* global_in
 int lama_resblocks_device(lama_engine* e, const float* d_local_in, const float* d_global_in, int batch, int h,
                           int w, int nblocks, float* d_local_out, float* d_global_out);
 
+/* Tile policy of the convolution GEMMs for plans built after this call
+ * (cached plans are dropped): LAMA_TILING_AUTO picks per launch,
+ * LAMA_TILING_SWAPPED uses channel-major tiles (M = 128 output channels,
+ * N = 256 pixels) wherever they apply, LAMA_TILING_PIXEL never does.  All
+ * policies compute the same function; tests use this to cover both kernels. */
+enum { LAMA_TILING_AUTO = 0, LAMA_TILING_SWAPPED = 1, LAMA_TILING_PIXEL = 2 };
+int lama_set_tiling(lama_engine* e, int policy);
+
 /* Message of the last failure on this engine ("" if none). */
 const char* lama_last_error(const lama_engine* e);
 

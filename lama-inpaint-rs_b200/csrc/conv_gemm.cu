@@ -13,11 +13,12 @@
 // product to ~2^-16 relative (the dropped lo*lo term and the 16-bit operand
 // rounding) at the BF16 tensor-core rate.
 //
-// Structure: persistent CTAs (one per SM), 256 threads:
+// Structure: persistent CTAs (one per SM), 384 threads:
 //   warp 0      TMA producer (one elected thread), STAGES-deep smem ring
 //   warp 1      MMA issuer (one thread): 4 K-steps x 3 MMAs per 64-wide K block
 //   warp 2      TMEM allocator
-//   warps 4..7  epilogue: tcgen05.ld 32 columns at a time, fused BN/bias,
+//   warps 4..11 epilogue (two warps per TMEM lane quarter, splitting the
+//               columns): tcgen05.ld 32 columns at a time, fused BN/bias,
 //               ReLU, residual, sigmoid, split-bf16 or fp32 store, reflect halo
 // TMEM holds two BN-column accumulators so the epilogue of one tile overlaps
 // the main loop of the next.
@@ -39,7 +40,9 @@ __host__ __device__ constexpr int stages_for(int bn) {
 // Extra shared memory of the shifted-sum epilogue (OUT_SHIFT7_NCHW):
 // two 128 x 33 fp32 staging tiles.
 constexpr int SHIFT_LD = 33;
-__host__ __device__ constexpr uint32_t extra_smem(int bn) { return bn == 32 ? 2u * 128u * SHIFT_LD * 4u : 0u; }
+__host__ __device__ constexpr uint32_t extra_smem(int bn) {
+  return bn == 32 ? 2u * 128u * SHIFT_LD * 4u : bn == 256 ? 8u * 32u * SHIFT_LD * 4u : 0u;
+}
 __host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 2 * A_PART + 2u * (uint32_t)bn * 128u; }
 __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
   return 2 * bn <= 32 ? 32 : 2 * bn <= 64 ? 64 : 2 * bn <= 128 ? 128 : 2 * bn <= 256 ? 256 : 512;
@@ -111,23 +114,12 @@ __device__ __forceinline__ void store_split(const GemmParams& p, int b, int oy, 
     }
 }
 
+// Residual, sigmoid and the store of CH channels [C.n0, C.n0 + CH) of one
+// output pixel whose values already carry the per-channel affine and ReLU.
 template <int CH>
-__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const GemmClass& C, int b, int oy, int ox,
-                                               int nloc, float* v) {
+__device__ __forceinline__ void store_channels(const GemmParams& p, const GemmClass& C, int b, int oy, int ox,
+                                               float* v, int nloc = 0) {
   const int n = C.n0 + nloc;
-#pragma unroll
-  for (int k = 0; k < CH; k++) {
-    int nn = n + k;
-    float s = 1.f, t = 0.f;
-    if (nloc + k < C.nvalid) {
-      s = __ldg(p.scale + nn);
-      t = __ldg(p.shift + nn);
-    }
-    float x = v[k] * s;
-    x = x + t;
-    if (p.relu) x = x > 0.f ? x : 0.f;
-    v[k] = x;
-  }
   if (p.skip) {
     const int hp = p.out_h + 2 * p.out_halo, wp = p.out_w + 2 * p.out_halo;
     long long off = (((long long)b * hp + oy + p.out_halo) * wp + ox + p.out_halo) * p.out_c + n;
@@ -168,8 +160,76 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const GemmCl
   }
 }
 
+template <int CH>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const GemmClass& C, int b, int oy, int ox,
+                                               int nloc, float* v) {
+  const int n = C.n0 + nloc;
+#pragma unroll
+  for (int k = 0; k < CH; k++) {
+    int nn = n + k;
+    float s = 1.f, t = 0.f;
+    if (nloc + k < C.nvalid) {
+      s = __ldg(p.scale + nn);
+      t = __ldg(p.shift + nn);
+    }
+    float x = v[k] * s;
+    x = x + t;
+    if (p.relu) x = x > 0.f ? x : 0.f;
+    v[k] = x;
+  }
+  store_channels<CH>(p, C, b, oy, ox, v, nloc);
+}
+
+// Swapped-tile epilogue: TMEM lane m holds output channel n0 + nt*128 + m for
+// the tile's BN pixels.  Each warp owns 32 channels; per 32-pixel chunk it
+// applies the per-channel affine + ReLU, transposes the 32 x 32 block through
+// its own shared-memory tile, and then every lane owns one pixel and stores the
+// warp's 32 channels as 16-byte vectors (with residual, split and halo), the
+// same store path as the pixel-major epilogue.
 template <int BN>
-__global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ GemmParams p) {
+__device__ __forceinline__ void epilogue_swapped(const GemmParams& p, const GemmClass& C, const TileInfo& ti, int m,
+                                                 uint32_t trow, float* tbuf, int half) {
+  const int lane = m & 31;
+  const int wch = ti.nt * 128 + (m & ~31);  // class-relative first channel of this warp
+  const int nloc = wch + lane;
+  const bool chv = nloc < C.nvalid;
+  const int n = C.n0 + nloc;
+  const float sc = chv ? __ldg(p.scale + n) : 0.f;
+  const float sh = chv ? __ldg(p.shift + n) : 0.f;
+#pragma unroll 1
+  for (int ch = half; ch < BN / 32; ch += 2) {
+    float v[32];
+    tmem_ld32(trow + ch * 32, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 32; q++) {
+      float x = v[q] * sc;
+      x = x + sh;
+      if (p.relu) x = x > 0.f ? x : 0.f;
+      tbuf[q * SHIFT_LD + lane] = x;  // [pixel][channel]
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 32; k++) v[k] = tbuf[lane * SHIFT_LD + k];
+    __syncwarp();
+    const int pix = ch * 32 + lane;
+    const int i = ti.i0 + pix / p.bw, j = ti.j0 + pix % p.bw;
+    if (i < p.mh && j < p.mw && wch < C.nvalid) {
+      const int oy = i * C.oy_mul + C.oy_add, ox = j * C.ox_mul + C.ox_add;
+      GemmClass Cn = C;  // affine already applied: run the store path with identity scale/shift
+      Cn.n0 = C.n0 + wch;
+      store_channels<32>(p, Cn, ti.b, oy, ox, v);
+    }
+  }
+}
+
+// SWAP = false: M = 128 pixels (A = activations), N = BN output channels (B = weights).
+// SWAP = true:  M = 128 output channels (A = weights), N = BN pixels (B = activations);
+//               more MACs per staged byte when the output has >= 128 channels
+//               (BN = 256: 65 MAC/B instead of 48 at BN = 128).  The epilogue then
+//               holds one output channel per thread and walks the tile's pixels.
+template <int BN, bool SWAP>
+__global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ GemmParams p) {
   constexpr int STAGES = stages_for(BN);
   constexpr uint32_t B_PART = (uint32_t)BN * 128u;
   constexpr uint32_t STAGE = stage_bytes(BN);
@@ -198,7 +258,7 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
     }
     for (int a = 0; a < 2; a++) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 128);
+      mbar_init(tempty_bar(a), 256);
     }
     fence_mbar_init();
   }
@@ -219,7 +279,7 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
     // ---------------------------------------------------------- producer
     if (lane == 0) {
       const int subs_per_kb = 64 / p.cb;
-      const uint32_t sub_bytes = (uint32_t)p.cb * 128u * 2u;
+      const uint32_t sub_bytes = (uint32_t)p.cb * (SWAP ? BN : 128u) * 2u;
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -231,6 +291,9 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
           if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(full_bar(stage), STAGE);
           const uint32_t sa = smem0 + (uint32_t)stage * STAGE;
+          // activation sub-boxes: the A operand, or the B operand when swapped
+          const uint32_t act = SWAP ? sa + 2 * A_PART : sa;
+          const uint32_t act_part = SWAP ? B_PART : A_PART;
           for (int u = 0; u < subs_per_kb; u++) {
             const int sub = kb * subs_per_kb + u;
             while (seg + 1 < C.nseg && sub >= C.seg[seg + 1].sub0) seg++;
@@ -240,11 +303,15 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
             const int cx = S.c0 + blk * p.cb;
             const int x = ti.j0 * S.stride + S.dx[tap];
             const int y = ti.i0 * S.stride + S.dy[tap];
-            tma_load_5d(sa + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, full_bar(stage));
-            tma_load_5d(sa + A_PART + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 1, full_bar(stage));
+            tma_load_5d(act + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, full_bar(stage));
+            tma_load_5d(act + act_part + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 1, full_bar(stage));
           }
-          tma_load_3d(sa + 2 * A_PART, &p.bmap[ti.cls], kb * 64, ti.nt * BN, 0, full_bar(stage));
-          tma_load_3d(sa + 2 * A_PART + B_PART, &p.bmap[ti.cls], kb * 64, ti.nt * BN, 1, full_bar(stage));
+          // weights: the B operand (BN rows), or the A operand (128 rows) when swapped
+          const uint32_t wdst = SWAP ? sa : sa + 2 * A_PART;
+          const uint32_t wpart = SWAP ? A_PART : B_PART;
+          const int wrow = SWAP ? ti.nt * 128 : ti.nt * BN;
+          tma_load_3d(wdst, &p.bmap[ti.cls], kb * 64, wrow, 0, full_bar(stage));
+          tma_load_3d(wdst + wpart, &p.bmap[ti.cls], kb * 64, wrow, 1, full_bar(stage));
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -252,7 +319,7 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const bool sw64 = (p.cb == 32);
+      const bool sw64 = !SWAP && (p.cb == 32);  // swapped A is the 128B-swizzled weight tile
       const uint32_t a_sbo = sw64 ? 512u : 1024u;
       const uint32_t a_layout = sw64 ? 4u : 2u;
       int stage = 0;
@@ -290,8 +357,10 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------- epilogue
+    // 8 warps: warp 4+q and 8+q share TMEM lanes 32q..32q+31 and split the columns
     const int ew = warp - 4;
-    const int m = ew * 32 + lane;
+    const int quarter = ew & 3, half = ew >> 2;
+    const int m = quarter * 32 + lane;
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, it++) {
       const TileInfo ti = decode_tile(p, t);
@@ -299,12 +368,23 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
       const int acc = it & 1;
       if (!mbar_wait(tfull_bar(acc), (it >> 1) & 1, p.err, 4)) break;
       tc_fence_after();
+      const uint32_t trow = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr (SWAP) {
+        epilogue_swapped<BN>(p, C, ti, m, trow, shift_buf + ew * 32 * SHIFT_LD, half);
+        tc_fence_before();
+        mbar_arrive(tempty_bar(acc));
+        continue;
+      }
       const int i = ti.i0 + m / p.bw, j = ti.j0 + m % p.bw;
       const bool valid = (i < p.mh) && (j < p.mw);
       const int oy = i * C.oy_mul + C.oy_add, ox = j * C.ox_mul + C.ox_add;
-      const uint32_t trow = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
       if constexpr (BN == 32) {
         if (p.out_kind == OUT_SHIFT7_NCHW) {
+          if (half) {  // one 32-column chunk: the first four epilogue warps take it
+            tc_fence_before();
+            mbar_arrive(tempty_bar(acc));
+            continue;
+          }
           float v[32];
           tmem_ld32(trow, v);
           tmem_wait_ld();
@@ -331,7 +411,7 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
         }
       }
 #pragma unroll 1
-      for (int ch = 0; ch < BN / CH; ch++) {
+      for (int ch = half; ch < BN / CH; ch += 2) {
         float v[CH];
         if constexpr (CH == 32) tmem_ld32(trow + ch * CH, v);
         else tmem_ld16(trow + ch * CH, v);
@@ -351,16 +431,16 @@ __global__ void __launch_bounds__(256, 1) k_conv_gemm(const __grid_constant__ Ge
   }
 }
 
-template <int BN>
+template <int BN, bool SWAP = false>
 int prepare_bn() {
   const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256 + extra_smem(BN);
-  return (int)cudaFuncSetAttribute(k_conv_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  return (int)cudaFuncSetAttribute(k_conv_gemm<BN, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 
-template <int BN>
+template <int BN, bool SWAP = false>
 int launch_bn(const GemmParams& p, int grid, cudaStream_t stream) {
   const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256 + extra_smem(BN);
-  k_conv_gemm<BN><<<grid, 256, smem, stream>>>(p);
+  k_conv_gemm<BN, SWAP><<<grid, 384, smem, stream>>>(p);
   return (int)cudaGetLastError();
 }
 
@@ -378,10 +458,12 @@ int conv_gemm_prepare() {
   if ((e = prepare_bn<64>())) return e;
   if ((e = prepare_bn<128>())) return e;
   if ((e = prepare_bn<192>())) return e;
+  if ((e = prepare_bn<256, true>())) return e;
   return prepare_bn<256>();
 }
 
 int launch_conv_gemm(const GemmParams& p, int bn, int grid, cudaStream_t stream) {
+  if (p.swap) return bn == 256 ? launch_bn<256, true>(p, grid, stream) : -1;
   switch (bn) {
     case 16: return launch_bn<16>(p, grid, stream);
     case 32: return launch_bn<32>(p, grid, stream);

@@ -480,10 +480,13 @@ struct OutSpec {
   const void* skip;
 };
 
-void choose_tile(int mh, int mw, int& bh, int& bw) {
+// Tile of `px` pixels (bh x bw) over an mh x mw grid, least padding waste;
+// TMA boxes cap each side at 256 / stride.
+void choose_tile(int mh, int mw, int& bh, int& bw, int px = 128, int stride = 1) {
   long long best = -1;
-  for (int cand = 128; cand >= 8; cand >>= 1) {
-    const int ch = 128 / cand;
+  for (int cand = px; cand >= 8; cand >>= 1) {
+    const int ch = px / cand;
+    if (cand * stride > 256 || ch * stride > 256) continue;
     const long long cost = (long long)((mh + ch - 1) / ch) * ch * ((mw + cand - 1) / cand) * cand;
     if (best < 0 || cost < best) {
       best = cost;
@@ -519,6 +522,7 @@ struct lama_engine {
   DevMem wmem;
   Weights W;
   int* d_err = nullptr;
+  int tiling = LAMA_TILING_AUTO;
   std::map<std::tuple<int, int, int, int, int, int, int>, std::unique_ptr<Plan>> plans;
 };
 
@@ -555,7 +559,7 @@ struct Builder {
 
   void gemm(const std::string& name, const GemmW& Wt, const std::vector<AmapSpec>& amaps,
             const std::vector<ClassSpec>& classes, int cb, int B, int mh, int mw, const OutSpec& o, int relu,
-            int sigmoid, double flops, int force_bn = 0, int step_x = 0) {
+            int sigmoid, double flops, int force_bn = 0, int step_x = 0, bool allow_swap = true) {
     Op op;
     op.kind = OP_GEMM;
     op.name = name;
@@ -563,8 +567,28 @@ struct Builder {
     op.g.reset(new GemmParams());
     GemmParams& p = *op.g;
     memset(&p, 0, sizeof(p));
+    int max_stride = 1;
+    for (auto& a : amaps) max_stride = std::max(max_stride, a.stride);
+    // Swapped tiles (M = 128 output channels, N = 256 pixels) stage more MACs per
+    // byte; used when every class has a multiple of 128 channels and the
+    // swapped tiling still gives every SM work.
+    bool swap = allow_swap && e.tiling != LAMA_TILING_PIXEL && step_x == 0 && force_bn == 0 && cb == 64 &&
+                (o.kind == OUT_SPLIT || o.kind == OUT_F32_NHWC);
+    for (auto& c : classes) swap = swap && c.nvalid % 128 == 0;
     int bh = 1, bw = 128;
-    if (step_x == 0) choose_tile(mh, mw, bh, bw);
+    if (swap) {
+      choose_tile(mh, mw, bh, bw, 256, max_stride);
+      long long t = 0;
+      for (auto& c : classes)
+        t += (long long)B * ((mh + bh - 1) / bh) * ((mw + bw - 1) / bw) * (c.nvalid / 128);
+      if (t < e.sms && e.tiling != LAMA_TILING_SWAPPED) swap = false;
+    }
+    if (!swap) {
+      bh = 1;
+      bw = 128;
+      if (step_x == 0) choose_tile(mh, mw, bh, bw, 128, max_stride);
+    }
+    p.swap = swap ? 1 : 0;
     p.cb = cb;
     p.batch = B;
     p.mh = mh;
@@ -577,7 +601,7 @@ struct Builder {
     p.m_tiles = B * p.tiles_y * p.tiles_x;
     std::vector<int> ns;
     for (auto& c : classes) ns.push_back(c.nvalid);
-    const int bn = force_bn ? force_bn : choose_bn(ns, p.m_tiles);
+    const int bn = swap ? 256 : force_bn ? force_bn : choose_bn(ns, p.m_tiles);
     if (!bn) throw EngineError{LAMA_EUNSUPPORTED, name + ": no tile width divides the output channels"};
     op.bn = bn;
     for (size_t i = 0; i < amaps.size(); i++)
@@ -589,10 +613,10 @@ struct Builder {
       const ClassSpec& cs = classes[ci];
       GemmClass& C = p.cls[ci];
       const WClass& wc = Wt.cls[cs.wc];
-      p.bmap[ci] = w_map(wc, bn);
+      p.bmap[ci] = w_map(wc, swap ? 128 : bn);
       C.n0 = cs.n0;
       C.nvalid = cs.nvalid;
-      C.ntiles_n = (cs.nvalid + bn - 1) / bn;
+      C.ntiles_n = swap ? cs.nvalid / 128 : (cs.nvalid + bn - 1) / bn;
       C.oy_mul = cs.oy_mul; C.oy_add = cs.oy_add; C.ox_mul = cs.ox_mul; C.ox_add = cs.ox_add;
       C.nseg = (int)cs.segs.size();
       int sub = 0;
@@ -1077,6 +1101,15 @@ int lama_resblocks_device(lama_engine* e, const float* d_local_in, const float* 
                           int w, int nblocks, float* d_local_out, float* d_global_out) {
   return resblocks_impl(e, d_local_in, d_global_in, batch, h, w, nblocks, d_local_out, d_global_out,
                         cudaMemcpyDeviceToDevice, cudaMemcpyDeviceToDevice, false);
+}
+
+int lama_set_tiling(lama_engine* e, int policy) {
+  return guarded(e, [&] {
+    if (policy < LAMA_TILING_AUTO || policy > LAMA_TILING_PIXEL) throw EngineError{LAMA_EINVAL, "unknown tiling policy"};
+    CK(cudaStreamSynchronize(e->stream));
+    e->plans.clear();
+    e->tiling = policy;
+  });
 }
 
 const char* lama_last_error(const lama_engine* e) { return e ? e->err.c_str() : "null engine"; }

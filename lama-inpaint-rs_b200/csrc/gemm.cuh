@@ -67,6 +67,7 @@ struct GemmParams {
   CUtensorMap bmap[GEMM_MAX_CLASSES];
   GemmClass cls[GEMM_MAX_CLASSES];
   int nclass;
+  int swap;                   // 1: M = 128 output channels, N = BN pixels (see conv_gemm.cu)
   int cb;                     // channels per A sub-box: 64 (128B swizzle) or 32 (64B swizzle)
   int batch, mh, mw;          // M space: images x rows x cols
   int bh, bw;                 // tile rows x cols, bh * bw == 128

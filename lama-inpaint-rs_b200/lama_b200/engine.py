@@ -57,6 +57,7 @@ SIGNATURES = [
                                       _f32p, _f32p]),
     ("lama_resblocks_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                              ctypes.c_int, _vp, _vp]),
+    ("lama_set_tiling", ctypes.c_int, [_vp, ctypes.c_int]),
     ("lama_last_error", ctypes.c_char_p, [_vp]),
     ("lama_synchronize", ctypes.c_int, [_vp]),
     ("lama_stream", _vp, [_vp]),
@@ -169,6 +170,12 @@ class Engine:
 
     def stream(self) -> int:
         return lib().lama_stream(self._h) or 0
+
+    TILING_AUTO, TILING_SWAPPED, TILING_PIXEL = 0, 1, 2
+
+    def set_tiling(self, policy: int):
+        """Tile policy for plans built from now on (see include/lama_b200.h)."""
+        self._check(lib().lama_set_tiling(self._h, policy))
 
     def synchronize(self):
         self._check(lib().lama_synchronize(self._h))

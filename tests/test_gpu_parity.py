@@ -184,3 +184,33 @@ def test_full_size_512_batch_properties(engine_baseline):
     assert np.isfinite(a).all() and a.min() >= 0 and a.max() <= 1
     np.testing.assert_array_equal(a[0], a[1])
     np.testing.assert_array_equal(a, engine_baseline.forward(xs))
+
+
+@pytest.mark.parametrize("policy", [1, 2])
+def test_tiling_policies_compute_the_same_pass(engine_tamed, oracle_tamed, policy):
+    """Channel-major (swapped) and pixel-major GEMM tiles both match the oracle."""
+    try:
+        engine_tamed.set_tiling(policy)
+        for h, w, seed in [(64, 64, 61), (72, 56, 62), (128, 96, 63)]:
+            _, _, x = make_input(h, w, seed)
+            got = engine_tamed.forward(x)
+            assert np.abs(got - oracle_tamed.forward(x)).max() <= FLOAT_TOL, (policy, h, w)
+        xs = np.stack([make_input(64, 64, s)[2] for s in (64, 65)])
+        np.testing.assert_array_equal(engine_tamed.forward(xs)[1], engine_tamed.forward(xs[1]))
+    finally:
+        engine_tamed.set_tiling(0)
+
+
+def test_swapped_tiles_match_pixel_tiles_on_the_baseline_stack(engine_baseline):
+    rng = np.random.default_rng(9)
+    l = rng.standard_normal((2, 128, 16, 16)).astype(np.float32)
+    g = rng.standard_normal((2, 384, 16, 16)).astype(np.float32)
+    try:
+        engine_baseline.set_tiling(1)
+        a = engine_baseline.resblocks(l, g, 18)
+        engine_baseline.set_tiling(2)
+        b = engine_baseline.resblocks(l, g, 18)
+    finally:
+        engine_baseline.set_tiling(0)
+    scale = max(np.abs(b[0]).max(), np.abs(b[1]).max())
+    assert np.abs(a[0] - b[0]).max() / scale < 1e-3 and np.abs(a[1] - b[1]).max() / scale < 1e-3
