@@ -368,7 +368,8 @@ def extra_timings(eng, stream):
         eng.synchronize()
         return e0.elapsed_time(e1) / k
 
-    for side, key in ((512, "ms_per_512_pass_b1"), (1024, "ms_per_1024_pass_b1"), (600, "ms_per_600_tile_pass_b1")):
+    for side, key in ((512, "ms_per_512_pass_b1"), (1024, "ms_per_1024_pass_b1"), (600, "ms_per_600_tile_pass_b1"),
+                      (2048, "ms_per_2048_pass_b1")):
         try:
             x = torch.rand((1, 4, side, side), device="cuda")
             y = torch.empty((1, 3, side, side), device="cuda")

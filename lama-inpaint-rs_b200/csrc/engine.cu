@@ -523,14 +523,21 @@ struct lama_engine {
   Weights W;
   int* d_err = nullptr;
   int tiling = LAMA_TILING_AUTO;
+  int spectral = LAMA_SPECTRAL_AUTO;
   std::map<std::tuple<int, int, int, int, int, int, int>, std::unique_ptr<Plan>> plans;
 };
 
 namespace {
 
+constexpr size_t kFftSmem = 160 * 1024;  // dynamic shared memory cap of the two-pass spectral kernels
+
 struct Builder {
   lama_engine& e;
   Plan& pl;
+
+  // The register-resident spectral kernels are the faster choice wherever
+  // they apply (measured at batch 1 and 32 on 64x64 planes).
+  bool use_reg_fft() const { return e.spectral != LAMA_SPECTRAL_TWO_PASS; }
 
   Act act(int B, int H, int W, int C, int halo) {
     Act a;
@@ -710,7 +717,6 @@ struct Builder {
     FftParams fp{};
     fp.batch = B; fp.c = 192; fp.h = h; fp.w = w; fp.wh = wh;
     fp.log2h = log2_or_neg(h); fp.log2w = log2_or_neg(w);
-    fp.lmax = std::max(h, w);
     fp.scale = (float)(1.0 / std::sqrt((double)h * (double)w));
     fp.tw_h = twiddles(h);
     fp.tw_w = twiddles(w);
@@ -720,13 +726,11 @@ struct Builder {
     fp.fu = fu;
     fp.s_out = S.p;
     fp.s_part = S.part();
-    const size_t budget = 200 * 1024;
-    const size_t fixed = sizeof(float2) * ((size_t)16 * fp.lmax + h + w);
-    const size_t per_ch = sizeof(float2) * (size_t)h * wh;
-    if (fixed + per_ch > budget)
+    if (!fft_tiles(fp, kFftSmem))
       throw EngineError{LAMA_EUNSUPPORTED, "latent plane " + std::to_string(h) + "x" + std::to_string(w) +
-                                               " is too large for the single-pass spectral kernels"};
-    fp.cg = (int)std::min<size_t>(8, (budget - fixed) / per_ch);
+                                               " needs more shared memory than the spectral kernels have"};
+    const bool reg = fft_reg_supported(h, w) && use_reg_fft();
+    if (!reg) fp.tmp = (float2*)pl.mem.alloc(fft_tmp_elems(fp) * sizeof(float2));
     const double px = (double)B * h * w, pxs = (double)B * h * wh;
     for (int blk = 0; blk < nblocks; blk++)
       for (int sub = 0; sub < 2; sub++) {
@@ -737,7 +741,6 @@ struct Builder {
         // conv1 1x1 384 -> 192 on the global channels, BN, ReLU -> feat (fp32)
         gemm("spectral_conv1", F.conv1, {{Xin, 1, false}}, {one_seg(0, 0, 192, SegSpec{0, 128, 384, 1, {{1, 1}}})}, 64, B, h, w,
              OutSpec{OUT_F32_NCHW, feat, 0, 192, h, w, 0, 0, nullptr}, 1, 0, 2.0 * px * 192 * 384);
-        const bool reg = fft_reg_supported(h, w);
         Op r;
         r.kind = reg ? OP_RFFT_REG : OP_RFFT;
         r.name = "rfft2";
@@ -1006,7 +1009,7 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
     e->sms = prop.multiProcessorCount;
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     CKL(conv_gemm_prepare());
-    CKL(fft_prepare(200 * 1024 + 4096));
+    CKL(fft_prepare(kFftSmem));
     CKL(fft_reg_prepare());
     e->d_err = (int*)e->wmem.alloc(256);
     upload_weights(e->W, e->wmem);
@@ -1109,6 +1112,15 @@ int lama_set_tiling(lama_engine* e, int policy) {
     CK(cudaStreamSynchronize(e->stream));
     e->plans.clear();
     e->tiling = policy;
+  });
+}
+
+int lama_set_spectral_path(lama_engine* e, int path) {
+  return guarded(e, [&] {
+    if (path < LAMA_SPECTRAL_AUTO || path > LAMA_SPECTRAL_REGISTER) throw EngineError{LAMA_EINVAL, "unknown spectral path"};
+    CK(cudaStreamSynchronize(e->stream));
+    e->plans.clear();
+    e->spectral = path;
   });
 }
 

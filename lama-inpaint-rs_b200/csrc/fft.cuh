@@ -11,8 +11,10 @@ struct FftParams {
   int batch, c;            // images, real channels (the spectrum has 2c)
   int h, w, wh;            // plane, wh = w/2 + 1
   int log2h, log2w;        // log2 of a power-of-two length, else -1
-  int cg;                  // channels per CTA
-  int lmax;                // max(h, w): line buffer length
+  int cg;                  // fft.cu: channels per CTA of the column and inverse-row passes
+  int kb;                  // fft.cu: columns (kx) per CTA of the column passes
+  int rp;                  // fft.cu: row pairs per CTA of the forward row pass
+  int rpi;                 // fft.cu: row pairs per CTA of the inverse row pass
   float scale;             // 1/sqrt(h*w)
   const float2* tw_h;      // (cos, sin)(2 pi k / h), k < h
   const float2* tw_w;      // (cos, sin)(2 pi k / w), k < w
@@ -22,9 +24,15 @@ struct FftParams {
   const float* fu;         // irfft2 in: fp32 [B][h][wh][2c]
   void* s_out;             // irfft2 out: split bf16 [2][B][h][w][c] = feat + irfft2(fu)
   long long s_part;
+  float2* tmp;             // fft.cu: intermediate, fft_tmp_elems(p) complex values
 };
 
-size_t fft_smem_bytes(const FftParams& p);
+// Two-pass kernels for any plane size (fft.cu).  fft_tiles fills cg/kb/rp/rpi
+// from c, h, w so that every pass fits max_smem (false if none does);
+// pass 0 = rows_fwd, 1 = the column passes, 2 = rows_inv.
+bool fft_tiles(FftParams& p, size_t max_smem);
+size_t fft_smem_bytes(const FftParams& p, int pass);
+size_t fft_tmp_elems(const FftParams& p);
 int fft_prepare(size_t max_smem);
 int launch_rfft2(const FftParams& p, cudaStream_t st);
 int launch_irfft2(const FftParams& p, cudaStream_t st);

@@ -58,6 +58,7 @@ SIGNATURES = [
     ("lama_resblocks_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                              ctypes.c_int, _vp, _vp]),
     ("lama_set_tiling", ctypes.c_int, [_vp, ctypes.c_int]),
+    ("lama_set_spectral_path", ctypes.c_int, [_vp, ctypes.c_int]),
     ("lama_last_error", ctypes.c_char_p, [_vp]),
     ("lama_synchronize", ctypes.c_int, [_vp]),
     ("lama_stream", _vp, [_vp]),
@@ -176,6 +177,12 @@ class Engine:
     def set_tiling(self, policy: int):
         """Tile policy for plans built from now on (see include/lama_b200.h)."""
         self._check(lib().lama_set_tiling(self._h, policy))
+
+    SPECTRAL_AUTO, SPECTRAL_TWO_PASS, SPECTRAL_REGISTER = 0, 1, 2
+
+    def set_spectral_path(self, path: int):
+        """Spectral-transform kernels for plans built from now on (see include/lama_b200.h)."""
+        self._check(lib().lama_set_spectral_path(self._h, path))
 
     def synchronize(self):
         self._check(lib().lama_synchronize(self._h))

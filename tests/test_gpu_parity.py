@@ -201,6 +201,47 @@ def test_tiling_policies_compute_the_same_pass(engine_tamed, oracle_tamed, polic
         engine_tamed.set_tiling(0)
 
 
+@pytest.mark.parametrize("path", [1, 2])
+def test_spectral_paths_compute_the_same_pass(engine_tamed, oracle_tamed, path):
+    """Two-pass and register-resident spectral kernels both match the oracle,
+    single images and a batch (the automatic choice depends on the batch)."""
+    try:
+        engine_tamed.set_spectral_path(path)
+        for h, w, seed in [(64, 64, 71), (128, 128, 72), (72, 56, 73)]:
+            _, _, x = make_input(h, w, seed)
+            assert np.abs(engine_tamed.forward(x) - oracle_tamed.forward(x)).max() <= FLOAT_TOL, (path, h, w)
+        xs = np.stack([make_input(64, 64, s)[2] for s in (74, 75)])
+        got = engine_tamed.forward(xs)
+        for i in range(2):
+            assert np.abs(got[i] - oracle_tamed.forward(xs[i])).max() <= FLOAT_TOL, (path, i)
+    finally:
+        engine_tamed.set_spectral_path(0)
+
+
+@pytest.mark.parametrize("h,w", [(1024, 1024), (2048, 2048), (600, 600), (520, 776)])
+def test_two_pass_spectral_kernels_on_large_latents(engine_tamed, h, w):
+    """rfft2 and irfft2 (+ the FourierUnit residual) of the first resblock at
+    latents 128^2, 256^2, 75^2 (the --tile window of
+    config 2) and 65x97 against float64 torch with the reference's transform
+    directions, on the engine's own conv1 / FourierUnit-conv outputs."""
+    from torch_ref import irfft2_ortho, rfft2_ortho
+    _, _, x = make_input(h, w, 81)
+    lh, lw = h // 8, w // 8
+    engine_tamed.debug_run(x, 9)
+    reads = {op: engine_tamed.debug_read(1, h, w, op) for op in (5, 6, 7, 8)}
+    assert [reads[op][0] for op in (5, 6, 7, 8)] == ["spectral_conv1", "rfft2", "fourier_conv", "irfft2"]
+    feat = torch.from_numpy(reads[5][1].reshape(1, 192, lh, lw)).double()
+    sp = rfft2_ortho(feat)
+    exp_spec = torch.stack((sp.real, sp.imag), -1).permute(0, 2, 3, 1, 4).reshape(1, lh, lw // 2 + 1, 384).numpy()
+    got_spec = reads[6][1].reshape(exp_spec.shape)
+    assert np.abs(got_spec - exp_spec).max() <= 1e-4 * np.abs(exp_spec).max()
+    fu = torch.from_numpy(reads[7][1].reshape(1, lh, lw // 2 + 1, 192, 2)).double()
+    fc = torch.complex(fu[..., 0], fu[..., 1]).permute(0, 3, 1, 2)
+    exp_s = (feat + irfft2_ortho(fc, lh, lw)).permute(0, 2, 3, 1).numpy()
+    got_s = reads[8][1].reshape(exp_s.shape)
+    assert np.abs(got_s - exp_s).max() <= 1e-4 * np.abs(exp_s).max()
+
+
 def test_swapped_tiles_match_pixel_tiles_on_the_baseline_stack(engine_baseline):
     rng = np.random.default_rng(9)
     l = rng.standard_normal((2, 128, 16, 16)).astype(np.float32)
