@@ -49,7 +49,8 @@ enum {
   LAMA_ECUDA = -3,    /* CUDA runtime / driver error */
   LAMA_EDEVICE = -4,  /* a kernel reported a device-side error (timeout, bad plan) */
   LAMA_ENOMEM = -5,   /* device allocation refused */
-  LAMA_EUNSUPPORTED = -6
+  LAMA_EUNSUPPORTED = -6,
+  LAMA_ESCRATCH = -7  /* lama_rfft2_noalloc: request larger than its fixed scratch array */
 };
 
 /* Open the safetensors weight file and build the engine on CUDA device
@@ -166,6 +167,24 @@ int lama_mask_depth(const uint8_t* mask, int w, int h, uint32_t* depth);
 /* The --sections pieces, rim first: up to `cap` rectangles {x0, y0, x1, y1}
  * (exclusive ends) written to `out`; returns their count (main.rs:597-659). */
 int lama_section_rects(const uint8_t* mask, int w, int h, int* out, int cap);
+
+/* No counterpart in the reference: the FourierUnit's forward transform
+ * (rfft2, norm='ortho', the reference's transform directions) on its own,
+ * for callers that cannot allocate device memory.  It runs the two-pass
+ * kernels with their intermediate in a fixed device array compiled into the
+ * library and calls no cudaMalloc / cudaFree.
+ *   d_feat: [batch][channels][h][w] fp32 (device);
+ *   d_spec: [2][batch][h][w/2+1][2*channels] bf16 (device), value = part 0 +
+ *           part 1, channel 2c = real and 2c+1 = imaginary part of channel c
+ *           (the engine's own spectrum layout).
+ * Limits: h, w <= 1024 and batch*channels*(w/2+1)*h <= 2,097,152 (16 MiB of
+ * complex fp32); larger requests return LAMA_ESCRATCH.  Work is queued on
+ * `stream` (a cudaStream_t, null = legacy default stream) of CUDA device
+ * `device`; the caller's current device is restored.  Every call shares the
+ * one array: calls whose GPU work overlaps in time race.  On failure a
+ * message is written to err (err_len bytes, may be null). */
+int lama_rfft2_noalloc(int device, const float* d_feat, int batch, int channels, int h, int w, void* d_spec,
+                       void* stream, char* err, int err_len);
 
 /* Free every device buffer and the engine. */
 void lama_close(lama_engine* e);

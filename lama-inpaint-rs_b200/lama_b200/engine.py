@@ -59,6 +59,8 @@ SIGNATURES = [
                                              ctypes.c_int, _vp, _vp]),
     ("lama_set_tiling", ctypes.c_int, [_vp, ctypes.c_int]),
     ("lama_set_spectral_path", ctypes.c_int, [_vp, ctypes.c_int]),
+    ("lama_rfft2_noalloc", ctypes.c_int, [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          _vp, _vp, ctypes.c_char_p, ctypes.c_int]),
     ("lama_last_error", ctypes.c_char_p, [_vp]),
     ("lama_synchronize", ctypes.c_int, [_vp]),
     ("lama_stream", _vp, [_vp]),
