@@ -170,12 +170,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--extra", action="store_true", help="also time 1024^2 / stack / tile passes")
     ap.add_argument("--single-pass", type=int, default=0, metavar="B",
-                    help="run one B-image 512^2 inpaint pass and exit (the case ncu captures)")
+                    help="run one B-image inpaint pass and exit (the case ncu captures)")
+    ap.add_argument("--size", type=int, default=SIZE, help="image side of --single-pass")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.single_pass:
-        return single_pass(args.single_pass)
+        return single_pass(args.single_pass, args.size)
 
     import numpy as np
     import torch
@@ -332,22 +333,22 @@ def main():
     return 0
 
 
-def single_pass(b):
-    """One u8 inpaint pass of b seeded 512^2 pairs on device 0 (no JSON)."""
+def single_pass(b, size=SIZE):
+    """One u8 inpaint pass of b seeded size^2 pairs on device 0 (no JSON)."""
     import numpy as np
     import torch
     from lama_b200 import Engine, seeded
     wpath = os.path.join(tempfile.gettempdir(), "lama_bench_single.safetensors")
     seeded.write_weights(wpath)
-    rgb, mask = make_data(min(b, N_DISTINCT), SIZE)
+    rgb, mask = make_data(min(b, N_DISTINCT), size)
     idx = np.arange(b) % len(rgb)
     r = torch.from_numpy(rgb[idx]).cuda()
     m = torch.from_numpy(mask[idx]).cuda()
     o = torch.empty_like(r)
     with Engine(wpath, 0) as eng:
-        eng.inpaint_u8_device(r.data_ptr(), m.data_ptr(), o.data_ptr(), b, SIZE, SIZE)
+        eng.inpaint_u8_device(r.data_ptr(), m.data_ptr(), o.data_ptr(), b, size, size)
         eng.synchronize()
-    log(f"single pass of {b} images done")
+    log(f"single pass of {b} images of {size}^2 done")
     return 0
 
 

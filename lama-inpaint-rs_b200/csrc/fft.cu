@@ -48,54 +48,158 @@ __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
   return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
 }
 
-// Position of element k of a line when it is loaded: bit-reversed for the
-// radix-2 stages, natural for the direct DFT.
-__device__ __forceinline__ int load_pos(int k, int log2n) {
-  return log2n > 0 ? (int)(__brev((unsigned)k) >> (32 - log2n)) : k;
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2(a.x * s, a.y * s); }
+// i * sign * z
+__device__ __forceinline__ float2 rot(float2 z, float sign) { return make_float2(-sign * z.y, sign * z.x); }
+
+// e^{sign * 2 pi i m / n} from the (cos, sin) table of length n
+__device__ __forceinline__ float2 twf(const float2* tw, int m, float sign) {
+  const float2 w = tw[m];
+  return make_float2(w.x, sign * w.y);
 }
 
-// Transforms `nl` lines of length n, line l at buf + l * ls.  Powers of two:
-// in place (loaded bit-reversed), returns buf.  Otherwise a direct DFT into
-// tmp, returns tmp.  `sign` -1: sum x_j e^{-2 pi i jk/n}, +1: e^{+...}; tw
-// holds (cos, sin)(2 pi m / n), m < n.  Ends with __syncthreads.
-__device__ float2* transform_lines(float2* buf, float2* tmp, int nl, int ls, int n, int log2n, const float2* tw,
-                                   float sign) {
-  if (log2n >= 0) {
-    const int hn = n >> 1, nb = nl * hn;
-    for (int s = 1; s <= log2n; s++) {
-      const int half = 1 << (s - 1), tstride = n >> s;
-      for (int t = threadIdx.x; t < nb; t += blockDim.x) {
-        const int l = t >> (log2n - 1), r = t & (hn - 1);
-        const int k = r & (half - 1), i = ((r >> (s - 1)) << s) + k;
-        float2* L = buf + l * ls;
-        float2 w = tw[k * tstride];
-        w.y *= sign;
-        const float2 v = cmul(L[i + half], w), u = L[i];
-        L[i] = make_float2(u.x + v.x, u.y + v.y);
-        L[i + half] = make_float2(u.x - v.x, u.y - v.y);
-      }
-      __syncthreads();
-    }
-    return buf;
+// In-register DFT of R points: X_k = sum_r v_r e^{sign 2 pi i rk/R}.
+template <int R>
+__device__ __forceinline__ void dft_small(float2 (&v)[R], float sign);
+
+template <>
+__device__ __forceinline__ void dft_small<2>(float2 (&v)[2], float) {
+  const float2 a = v[0], b = v[1];
+  v[0] = cadd(a, b);
+  v[1] = csub(a, b);
+}
+
+template <>
+__device__ __forceinline__ void dft_small<4>(float2 (&v)[4], float sign) {
+  const float2 s02 = cadd(v[0], v[2]), d02 = csub(v[0], v[2]);
+  const float2 s13 = cadd(v[1], v[3]), d13 = rot(csub(v[1], v[3]), sign);
+  v[0] = cadd(s02, s13);
+  v[2] = csub(s02, s13);
+  v[1] = cadd(d02, d13);
+  v[3] = csub(d02, d13);
+}
+
+template <>
+__device__ __forceinline__ void dft_small<8>(float2 (&v)[8], float sign) {
+  float2 e[4] = {v[0], v[2], v[4], v[6]}, o[4] = {v[1], v[3], v[5], v[7]};
+  dft_small<4>(e, sign);
+  dft_small<4>(o, sign);
+  constexpr float h = 0.70710678118654752f;  // cos(pi/4)
+  const float2 o1 = make_float2(h * (o[1].x - sign * o[1].y), h * (o[1].y + sign * o[1].x));
+  const float2 o2 = rot(o[2], sign);
+  const float2 o3 = make_float2(-h * (o[3].x + sign * o[3].y), h * (sign * o[3].x - o[3].y));
+  v[0] = cadd(e[0], o[0]);
+  v[4] = csub(e[0], o[0]);
+  v[1] = cadd(e[1], o1);
+  v[5] = csub(e[1], o1);
+  v[2] = cadd(e[2], o2);
+  v[6] = csub(e[2], o2);
+  v[3] = cadd(e[3], o3);
+  v[7] = csub(e[3], o3);
+}
+
+template <>
+__device__ __forceinline__ void dft_small<3>(float2 (&v)[3], float sign) {
+  constexpr float c = -0.5f, s = 0.86602540378443865f;  // cos, sin(2 pi / 3)
+  const float2 t = cadd(v[1], v[2]), d = rot(cscale(csub(v[1], v[2]), s), sign);
+  const float2 m = make_float2(v[0].x + c * t.x, v[0].y + c * t.y);
+  v[0] = cadd(v[0], t);
+  v[1] = cadd(m, d);
+  v[2] = csub(m, d);
+}
+
+template <>
+__device__ __forceinline__ void dft_small<5>(float2 (&v)[5], float sign) {
+  constexpr float c1 = 0.30901699437494742f, c2 = -0.80901699437494742f;  // cos(2 pi / 5), cos(4 pi / 5)
+  constexpr float s1 = 0.95105651629515357f, s2 = 0.58778525229247313f;   // sin(2 pi / 5), sin(4 pi / 5)
+  const float2 a1 = cadd(v[1], v[4]), b1 = csub(v[1], v[4]);
+  const float2 a2 = cadd(v[2], v[3]), b2 = csub(v[2], v[3]);
+  const float2 m1 = make_float2(v[0].x + c1 * a1.x + c2 * a2.x, v[0].y + c1 * a1.y + c2 * a2.y);
+  const float2 m2 = make_float2(v[0].x + c2 * a1.x + c1 * a2.x, v[0].y + c2 * a1.y + c1 * a2.y);
+  const float2 n1 = rot(make_float2(s1 * b1.x + s2 * b2.x, s1 * b1.y + s2 * b2.y), sign);
+  const float2 n2 = rot(make_float2(s2 * b1.x - s1 * b2.x, s2 * b1.y - s1 * b2.y), sign);
+  v[0] = cadd(v[0], cadd(a1, a2));
+  v[1] = cadd(m1, n1);
+  v[4] = csub(m1, n1);
+  v[2] = cadd(m2, n2);
+  v[3] = csub(m2, n2);
+}
+
+// One Stockham autosort stage of radix R over nl lines of length n (line l
+// at src/dst + l * ls); Ns = product of the radices already applied.
+// Butterfly j reads src[j + r n/R], twiddles input r by
+// e^{sign 2 pi i r (j mod Ns) / (Ns R)}, and writes its R-point DFT to
+// dst[(j / Ns) Ns R + (j mod Ns) + k Ns].
+template <int R>
+__device__ __forceinline__ void stage(const float2* src, float2* dst, int nl, int ls, int n, int Ns,
+                                      const float2* tw, float sign) {
+  const int m = n / R, nb = nl * m, tstep = n / (Ns * R);
+  for (int t = threadIdx.x; t < nb; t += blockDim.x) {
+    const int l = t / m, j = t - l * m, jm = j % Ns;
+    const float2* S = src + l * ls + j;
+    float2 v[R];
+    v[0] = S[0];
+#pragma unroll
+    for (int r = 1; r < R; r++) v[r] = cmul(S[r * m], twf(tw, r * jm * tstep, sign));
+    dft_small<R>(v, sign);
+    float2* D = dst + l * ls + (j - jm) * R + jm;
+#pragma unroll
+    for (int k = 0; k < R; k++) D[k * Ns] = v[k];
   }
+}
+
+// Stage of any radix R: every thread computes single outputs as length-R sums
+// (used for prime factors above 5, including a prime length itself, where it
+// is the direct DFT).
+__device__ void stage_generic(const float2* src, float2* dst, int nl, int ls, int n, int Ns, int R,
+                              const float2* tw, float sign) {
+  const int m = n / R, tstep = n / (Ns * R);
   for (int t = threadIdx.x; t < nl * n; t += blockDim.x) {
-    const int l = t / n, k = t - l * n;
-    const float2* L = buf + l * ls;
-    float2 acc = make_float2(0.f, 0.f);
-    int idx = 0;
-    for (int j = 0; j < n; j++) {
-      float2 w = tw[idx];
-      w.y *= sign;
-      const float2 v = cmul(L[j], w);
+    const int l = t / n, q = t - l * n;
+    const int jm = q % Ns, k = (q / Ns) % R, j = (q / (Ns * R)) * Ns + jm;
+    const float2* S = src + l * ls + j;
+    const int step = (tstep * (jm + k * Ns)) % n;
+    float2 acc = S[0];
+    int idx = step;
+    for (int r = 1; r < R; r++) {
+      const float2 v = cmul(S[r * m], twf(tw, idx, sign));
       acc.x += v.x;
       acc.y += v.y;
-      idx += k;
+      idx += step;
       if (idx >= n) idx -= n;
     }
-    tmp[l * ls + k] = acc;
+    dst[l * ls + q] = acc;
   }
-  __syncthreads();
-  return tmp;
+}
+
+// Transforms nl lines of length n held at a (line l at a + l * ls), ping-
+// ponging with b; returns the buffer holding the result (natural order).
+// `sign` -1: sum x_j e^{-2 pi i jk/n}, +1: e^{+...}; tw holds
+// (cos, sin)(2 pi m / n), m < n; `rad` lists the radices (product n).
+// Ends with __syncthreads.
+__device__ float2* transform_lines(float2* a, float2* b, int nl, int ls, int n, const Radices& rad,
+                                   const float2* tw, float sign) {
+  float2 *src = a, *dst = b;
+  int Ns = 1;
+  for (int s = 0; s < rad.n; s++) {
+    const int R = rad.r[s];
+    switch (R) {
+      case 2: stage<2>(src, dst, nl, ls, n, Ns, tw, sign); break;
+      case 3: stage<3>(src, dst, nl, ls, n, Ns, tw, sign); break;
+      case 4: stage<4>(src, dst, nl, ls, n, Ns, tw, sign); break;
+      case 5: stage<5>(src, dst, nl, ls, n, Ns, tw, sign); break;
+      case 8: stage<8>(src, dst, nl, ls, n, Ns, tw, sign); break;
+      default: stage_generic(src, dst, nl, ls, n, Ns, R, tw, sign); break;
+    }
+    __syncthreads();
+    float2* t = src;
+    src = dst;
+    dst = t;
+    Ns *= R;
+  }
+  return src;
 }
 
 __device__ __forceinline__ float direction(int log2n, bool inverse) {
@@ -124,10 +228,10 @@ __global__ void __launch_bounds__(kThreads) k_rows_fwd(const FftParams p) {
     const int l = t / W, x = t - l * W;
     const float a = plane[(size_t)(2 * l) * W + x];
     const float bb = 2 * l + 1 < nrows ? plane[(size_t)(2 * l + 1) * W + x] : 0.f;
-    buf[l * ls + load_pos(x, p.log2w)] = make_float2(a, bb);
+    buf[l * ls + x] = make_float2(a, bb);
   }
   __syncthreads();
-  const float2* L = transform_lines(buf, tmp, nl, ls, W, p.log2w, tw, direction(p.log2w, false));
+  const float2* L = transform_lines(buf, tmp, nl, ls, W, p.rad_w, tw, direction(p.log2w, false));
   // untangle the two real rows; T[b][c][kx][y], y fastest
   float2* T = p.tmp + ((size_t)b * p.c + c) * p.wh * p.h + y0;
   for (int t = threadIdx.x; t < p.wh * nrows; t += blockDim.x) {
@@ -153,10 +257,10 @@ __global__ void __launch_bounds__(kThreads) k_cols_fwd(const FftParams p) {
     const int l = t / H, y = t - l * H;
     const int kl = l / ncg, cl = l - kl * ncg;
     const float2 v = p.tmp[(((size_t)b * p.c + c0 + cl) * p.wh + kx0 + kl) * H + y];
-    buf[l * ls + load_pos(y, p.log2h)] = v;
+    buf[l * ls + y] = v;
   }
   __syncthreads();
-  const float2* L = transform_lines(buf, tmp, nl, ls, H, p.log2h, tw, direction(p.log2h, false));
+  const float2* L = transform_lines(buf, tmp, nl, ls, H, p.rad_h, tw, direction(p.log2h, false));
   // spectrum [b][ky][kx][2c + part], channel fastest
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.spec);
   const int C2 = 2 * p.c;
@@ -187,10 +291,10 @@ __global__ void __launch_bounds__(kThreads) k_cols_inv(const FftParams p) {
     const int cl = t % ncg, r = t / ncg, kl = r % nkb, ky = r / nkb;
     const float2 v = *reinterpret_cast<const float2*>(p.fu + (((size_t)b * H + ky) * p.wh + kx0 + kl) * C2 +
                                                       2 * (c0 + cl));
-    buf[(kl * ncg + cl) * ls + load_pos(ky, p.log2h)] = v;
+    buf[(kl * ncg + cl) * ls + ky] = v;
   }
   __syncthreads();
-  const float2* L = transform_lines(buf, tmp, nl, ls, H, p.log2h, tw, direction(p.log2h, true));
+  const float2* L = transform_lines(buf, tmp, nl, ls, H, p.rad_h, tw, direction(p.log2h, true));
   // T[b][y][kx][c], channel fastest
   for (int t = threadIdx.x; t < nl * H; t += blockDim.x) {
     const int cl = t % ncg, r = t / ncg, kl = r % nkb, y = r / nkb;
@@ -208,7 +312,6 @@ __global__ void __launch_bounds__(kThreads) k_rows_inv(const FftParams p) {
   float2* tw = sm;
   float2* buf = tw + W;
   float2* tmp = buf + p.rpi * p.cg * ls;
-  float* fe = reinterpret_cast<float*>(p.log2w >= 0 ? tmp : tmp + p.rpi * p.cg * ls);  // [row][channel][x]
   load_tw(tw, p.tw_w, W);
   // Hermitian completion of each row's bins; line (pair, channel) = row a + i row b
   for (int t = threadIdx.x; t < nl * W; t += blockDim.x) {
@@ -227,15 +330,17 @@ __global__ void __launch_bounds__(kThreads) k_rows_inv(const FftParams p) {
       a.y = -a.y;
       bb.y = -bb.y;
     }
-    buf[(pr * ncg + cl) * ls + load_pos(k, p.log2w)] = make_float2(a.x - bb.y, a.y + bb.x);
+    buf[(pr * ncg + cl) * ls + k] = make_float2(a.x - bb.y, a.y + bb.x);
   }
-  // feat rows of this tile, coalesced along x
+  __syncthreads();
+  const float2* L = transform_lines(buf, tmp, nl, ls, W, p.rad_w, tw, direction(p.log2w, true));
+  // feat rows of this tile, coalesced along x, into the buffer the result is not in
+  float* fe = reinterpret_cast<float*>(L == buf ? tmp : buf);  // [row][channel][x]
   for (int t = threadIdx.x; t < nrows * ncg * W; t += blockDim.x) {
     const int x = t % W, r = t / W, cl = r % ncg, row = r / ncg;
     fe[(row * ncg + cl) * fs + x] = p.feat[(((size_t)b * p.c + c0 + cl) * p.h + y0 + row) * W + x];
   }
   __syncthreads();
-  const float2* L = transform_lines(buf, tmp, nl, ls, W, p.log2w, tw, direction(p.log2w, true));
   // S [b][y][x][c] = feat + scale * row, channel fastest
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.s_out);
   for (int t = threadIdx.x; t < nrows * W * ncg; t += blockDim.x) {
@@ -254,21 +359,53 @@ inline size_t tw_bytes(int n) { return sizeof(float2) * (size_t)n; }
 }  // namespace
 
 size_t fft_smem_bytes(const FftParams& p, int pass) {
-  const bool pw = p.log2w >= 0, ph = p.log2h >= 0;
+  // twiddle table + two line buffers (the Stockham stages ping-pong)
   switch (pass) {
     case 0:  // rows_fwd
-      return tw_bytes(p.w) + (pw ? 1 : 2) * sizeof(float2) * (size_t)p.rp * (p.w + 1);
+      return tw_bytes(p.w) + 2 * sizeof(float2) * (size_t)p.rp * (p.w + 1);
     case 1:  // cols_fwd / cols_inv
-      return tw_bytes(p.h) + (ph ? 1 : 2) * sizeof(float2) * (size_t)p.cg * p.kb * (p.h + 1);
-    default:  // rows_inv: lines (+ tmp) + feat rows
-      return tw_bytes(p.w) + (pw ? 1 : 2) * sizeof(float2) * (size_t)p.rpi * p.cg * (p.w + 1) +
-             sizeof(float) * (size_t)2 * p.rpi * p.cg * (p.w + 1);
+      return tw_bytes(p.h) + 2 * sizeof(float2) * (size_t)p.cg * p.kb * (p.h + 1);
+    default:  // rows_inv (the feat rows reuse the free buffer)
+      return tw_bytes(p.w) + 2 * sizeof(float2) * (size_t)p.rpi * p.cg * (p.w + 1);
   }
+}
+
+// Radices of one line length: eights (a final 8 x 2 becomes 4 x 4), a four or
+// a two, then threes, fives and any other prime factors.
+Radices fft_radices(int n) {
+  Radices r{};
+  auto push = [&r](int f) { r.r[r.n++] = f; };
+  int k = 0;
+  while (n % 2 == 0) {
+    n /= 2;
+    k++;
+  }
+  while (k >= 3) {
+    push(8);
+    k -= 3;
+  }
+  if (k == 2) push(4);
+  if (k == 1) {
+    if (r.n > 0) {
+      r.r[r.n - 1] = 4;
+      push(4);
+    } else {
+      push(2);
+    }
+  }
+  for (int f = 3; n > 1; f += 2)
+    while (n % f == 0) {
+      push(f);
+      n /= f;
+    }
+  return r;
 }
 
 bool fft_tiles(FftParams& p, size_t max_smem) {
   constexpr int kElems = 4096;  // complex values per tile
   const int w = std::max(1, p.w), h = std::max(1, p.h), pairs = (h + 1) / 2;
+  p.rad_h = fft_radices(h);
+  p.rad_w = fft_radices(w);
   p.rp = std::max(1, std::min(kElems / w, pairs));
   for (p.cg = std::min(16, p.c); p.cg >= 1; p.cg /= 2) {
     p.kb = std::max(1, std::min(kElems / (p.cg * h), p.wh));

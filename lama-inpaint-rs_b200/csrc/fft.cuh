@@ -7,6 +7,12 @@
 
 namespace lama {
 
+// Stockham stage radices of one line length (product = the length).
+struct Radices {
+  int n;
+  int r[16];
+};
+
 struct FftParams {
   int batch, c;            // images, real channels (the spectrum has 2c)
   int h, w, wh;            // plane, wh = w/2 + 1
@@ -25,12 +31,14 @@ struct FftParams {
   void* s_out;             // irfft2 out: split bf16 [2][B][h][w][c] = feat + irfft2(fu)
   long long s_part;
   float2* tmp;             // fft.cu: intermediate, fft_tmp_elems(p) complex values
+  Radices rad_h, rad_w;    // fft.cu: stage radices of the column / row transforms
 };
 
 // Two-pass kernels for any plane size (fft.cu).  fft_tiles fills cg/kb/rp/rpi
 // from c, h, w so that every pass fits max_smem (false if none does);
 // pass 0 = rows_fwd, 1 = the column passes, 2 = rows_inv.
 bool fft_tiles(FftParams& p, size_t max_smem);
+Radices fft_radices(int n);
 size_t fft_smem_bytes(const FftParams& p, int pass);
 size_t fft_tmp_elems(const FftParams& p);
 int fft_prepare(size_t max_smem);
