@@ -133,18 +133,19 @@ __device__ __forceinline__ void dft_small<5>(float2 (&v)[5], float sign) {
 // e^{sign 2 pi i r (j mod Ns) / (Ns R)}, and writes its R-point DFT to
 // dst[(j / Ns) Ns R + (j mod Ns) + k Ns].
 template <int R>
-__device__ __forceinline__ void stage(const float2* src, float2* dst, int nl, int ls, int n, int Ns,
+__device__ __forceinline__ void stage(const float2* src, float2* dst, int nl, int ls, int n, const FftStage& sg,
                                       const float2* tw, float sign) {
-  const int m = n / R, nb = nl * m, tstep = n / (Ns * R);
+  const int m = (int)sg.m.d, Ns = (int)sg.ns.d, nb = nl * m, tstep = n / (Ns * R);
   for (int t = threadIdx.x; t < nb; t += blockDim.x) {
-    const int l = t / m, j = t - l * m, jm = j % Ns;
+    const int l = (int)fdiv(t, sg.m), j = t - l * m;
+    const int jq = (int)fdiv(j, sg.ns), jm = j - jq * Ns;
     const float2* S = src + l * ls + j;
     float2 v[R];
     v[0] = S[0];
 #pragma unroll
     for (int r = 1; r < R; r++) v[r] = cmul(S[r * m], twf(tw, r * jm * tstep, sign));
     dft_small<R>(v, sign);
-    float2* D = dst + l * ls + (j - jm) * R + jm;
+    float2* D = dst + l * ls + jq * Ns * R + jm;
 #pragma unroll
     for (int k = 0; k < R; k++) D[k * Ns] = v[k];
   }
@@ -153,12 +154,13 @@ __device__ __forceinline__ void stage(const float2* src, float2* dst, int nl, in
 // Stage of any radix R: every thread computes single outputs as length-R sums
 // (used for prime factors above 5, including a prime length itself, where it
 // is the direct DFT).
-__device__ void stage_generic(const float2* src, float2* dst, int nl, int ls, int n, int Ns, int R,
-                              const float2* tw, float sign) {
-  const int m = n / R, tstep = n / (Ns * R);
+__device__ void stage_generic(const float2* src, float2* dst, int nl, int ls, int n, const Radices& rad,
+                              const FftStage& sg, const float2* tw, float sign) {
+  const int R = sg.r, Ns = (int)sg.ns.d, m = (int)sg.m.d, tstep = n / (Ns * R);
   for (int t = threadIdx.x; t < nl * n; t += blockDim.x) {
-    const int l = t / n, q = t - l * n;
-    const int jm = q % Ns, k = (q / Ns) % R, j = (q / (Ns * R)) * Ns + jm;
+    const int l = (int)fdiv(t, rad.len), q = t - l * n;
+    const int qn = (int)fdiv(q, sg.ns), jm = q - qn * Ns;
+    const int qr = (int)fdiv(qn, sg.rr), k = qn - qr * R, j = qr * Ns + jm;
     const float2* S = src + l * ls + j;
     const int step = (tstep * (jm + k * Ns)) % n;
     float2 acc = S[0];
@@ -177,27 +179,27 @@ __device__ void stage_generic(const float2* src, float2* dst, int nl, int ls, in
 // Transforms nl lines of length n held at a (line l at a + l * ls), ping-
 // ponging with b; returns the buffer holding the result (natural order).
 // `sign` -1: sum x_j e^{-2 pi i jk/n}, +1: e^{+...}; tw holds
-// (cos, sin)(2 pi m / n), m < n; `rad` lists the radices (product n).
+// (cos, sin)(2 pi m / n), m < n; `rad` lists the stages (radix product n).
 // Ends with __syncthreads.
-__device__ float2* transform_lines(float2* a, float2* b, int nl, int ls, int n, const Radices& rad,
-                                   const float2* tw, float sign) {
+__device__ float2* transform_lines(float2* a, float2* b, int nl, int ls, const Radices& rad, const float2* tw,
+                                   float sign) {
   float2 *src = a, *dst = b;
-  int Ns = 1;
-  for (int s = 0; s < rad.n; s++) {
-    const int R = rad.r[s];
+  const int n = rad.n;
+  for (int s = 0; s < 12; s++) {
+    const int R = rad.st[s].r;
+    if (R == 0) break;
     switch (R) {
-      case 2: stage<2>(src, dst, nl, ls, n, Ns, tw, sign); break;
-      case 3: stage<3>(src, dst, nl, ls, n, Ns, tw, sign); break;
-      case 4: stage<4>(src, dst, nl, ls, n, Ns, tw, sign); break;
-      case 5: stage<5>(src, dst, nl, ls, n, Ns, tw, sign); break;
-      case 8: stage<8>(src, dst, nl, ls, n, Ns, tw, sign); break;
-      default: stage_generic(src, dst, nl, ls, n, Ns, R, tw, sign); break;
+      case 2: stage<2>(src, dst, nl, ls, n, rad.st[s], tw, sign); break;
+      case 3: stage<3>(src, dst, nl, ls, n, rad.st[s], tw, sign); break;
+      case 4: stage<4>(src, dst, nl, ls, n, rad.st[s], tw, sign); break;
+      case 5: stage<5>(src, dst, nl, ls, n, rad.st[s], tw, sign); break;
+      case 8: stage<8>(src, dst, nl, ls, n, rad.st[s], tw, sign); break;
+      default: stage_generic(src, dst, nl, ls, n, rad, rad.st[s], tw, sign); break;
     }
     __syncthreads();
     float2* t = src;
     src = dst;
     dst = t;
-    Ns *= R;
   }
   return src;
 }
@@ -208,34 +210,91 @@ __device__ __forceinline__ float direction(int log2n, bool inverse) {
   return fwd ? -1.f : 1.f;
 }
 
+// Loads items 0..total-1 U at a time per thread (all U global loads issued
+// before any shared-memory store, so each thread keeps U requests in flight).
+template <int U, class Ld, class St>
+__device__ __forceinline__ void batched(int total, Ld ld, St st) {
+  using V = decltype(ld(0));
+  for (int base = threadIdx.x; base < total; base += blockDim.x * U) {
+    V v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int i = base + u * (int)blockDim.x;
+      if (i < total) v[u] = ld(i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int i = base + u * (int)blockDim.x;
+      if (i < total) st(i, v[u]);
+    }
+  }
+}
+
+struct F4x2 {
+  float4 a, b;
+};
+
+__device__ __forceinline__ bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15) == 0; }
+
 __device__ __forceinline__ void load_tw(float2* dst, const float2* src, int n) {
   for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
 }
 
 // ------------------------------------------------------------------ rfft2
-// grid (row-pair blocks, c, b); lines = pairs of rows (a + i b), ls = w + 1
+// Every CTA works on a full tile (lines past the plane's edge are zero-filled
+// and never stored), so all index arithmetic uses plan-time divisors.
+
+// grid (row-pair blocks of rp, c, b); lines = pairs of rows (a + i b), ls = w + 1
 __global__ void __launch_bounds__(kThreads) k_rows_fwd(const FftParams p) {
   extern __shared__ __align__(16) float2 sm[];
   const int b = blockIdx.z, c = blockIdx.y, y0 = blockIdx.x * 2 * p.rp;
-  const int W = p.w, ls = W + 1;
-  const int nrows = min(2 * p.rp, p.h - y0), nl = (nrows + 1) >> 1;
+  const int W = p.w, ls = W + 1, R2 = 2 * p.rp;
+  const int nrows = min(R2, p.h - y0);
   float2* tw = sm;
   float2* buf = tw + W;
   float2* tmp = buf + p.rp * ls;
   load_tw(tw, p.tw_w, W);
   const float* plane = p.feat + (((size_t)b * p.c + c) * p.h + y0) * W;
-  for (int t = threadIdx.x; t < nl * W; t += blockDim.x) {
-    const int l = t / W, x = t - l * W;
-    const float a = plane[(size_t)(2 * l) * W + x];
-    const float bb = 2 * l + 1 < nrows ? plane[(size_t)(2 * l + 1) * W + x] : 0.f;
-    buf[l * ls + x] = make_float2(a, bb);
+  if ((W & 3) == 0 && aligned16(p.feat)) {
+    const int W4 = W >> 2;
+    batched<4>(
+        p.rp * W4,
+        [&](int t) {
+          const int l = t / W4, x = (t - l * W4) * 4;
+          const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+          F4x2 v{z, z};
+          if (2 * l < nrows) v.a = *reinterpret_cast<const float4*>(plane + (size_t)(2 * l) * W + x);
+          if (2 * l + 1 < nrows) v.b = *reinterpret_cast<const float4*>(plane + (size_t)(2 * l + 1) * W + x);
+          return v;
+        },
+        [&](int t, const F4x2& v) {
+          const int l = t / W4, x = (t - l * W4) * 4;
+          float2* d = buf + l * ls + x;
+          d[0] = make_float2(v.a.x, v.b.x);
+          d[1] = make_float2(v.a.y, v.b.y);
+          d[2] = make_float2(v.a.z, v.b.z);
+          d[3] = make_float2(v.a.w, v.b.w);
+        });
+  } else {
+    batched<8>(
+        p.rp * W,
+        [&](int t) {
+          const int l = (int)fdiv(t, p.fd_w), x = t - l * W;
+          return make_float2(2 * l < nrows ? plane[(size_t)(2 * l) * W + x] : 0.f,
+                             2 * l + 1 < nrows ? plane[(size_t)(2 * l + 1) * W + x] : 0.f);
+        },
+        [&](int t, float2 v) {
+          const int l = (int)fdiv(t, p.fd_w);
+          buf[l * ls + t - l * W] = v;
+        });
   }
   __syncthreads();
-  const float2* L = transform_lines(buf, tmp, nl, ls, W, p.rad_w, tw, direction(p.log2w, false));
+  const float2* L = transform_lines(buf, tmp, p.rp, ls, p.rad_w, tw, direction(p.log2w, false));
   // untangle the two real rows; T[b][c][kx][y], y fastest
   float2* T = p.tmp + ((size_t)b * p.c + c) * p.wh * p.h + y0;
-  for (int t = threadIdx.x; t < p.wh * nrows; t += blockDim.x) {
-    const int kx = t / nrows, r = t - kx * nrows, l = r >> 1;
+  for (int t = threadIdx.x; t < p.wh * R2; t += blockDim.x) {
+    const int kx = (int)fdiv(t, p.fd_rows), r = t - kx * R2, l = r >> 1;
+    if (r >= nrows) continue;
     const float2 zk = L[l * ls + kx], zm = L[l * ls + (kx == 0 ? 0 : W - kx)];
     T[(size_t)kx * p.h + r] = (r & 1) ? make_float2(0.5f * (zk.y + zm.y), -0.5f * (zk.x - zm.x))
                                       : make_float2(0.5f * (zk.x + zm.x), 0.5f * (zk.y - zm.y));
@@ -247,26 +306,34 @@ __global__ void __launch_bounds__(kThreads) k_rows_fwd(const FftParams p) {
 __global__ void __launch_bounds__(kThreads) k_cols_fwd(const FftParams p) {
   extern __shared__ __align__(16) float2 sm[];
   const int b = blockIdx.z, c0 = blockIdx.y * p.cg, kx0 = blockIdx.x * p.kb;
-  const int H = p.h, ls = H + 1;
-  const int ncg = min(p.cg, p.c - c0), nkb = min(p.kb, p.wh - kx0), nl = ncg * nkb;
+  const int H = p.h, ls = H + 1, CG = p.cg, nl = CG * p.kb;
+  const int ncg = min(CG, p.c - c0), nkb = min(p.kb, p.wh - kx0);
   float2* tw = sm;
   float2* buf = tw + H;
-  float2* tmp = buf + p.cg * p.kb * ls;
+  float2* tmp = buf + nl * ls;
   load_tw(tw, p.tw_h, H);
-  for (int t = threadIdx.x; t < nl * H; t += blockDim.x) {
-    const int l = t / H, y = t - l * H;
-    const int kl = l / ncg, cl = l - kl * ncg;
-    const float2 v = p.tmp[(((size_t)b * p.c + c0 + cl) * p.wh + kx0 + kl) * H + y];
-    buf[l * ls + y] = v;
-  }
+  batched<8>(
+      nl * H,
+      [&](int t) {
+        const int l = (int)fdiv(t, p.fd_h), y = t - l * H;
+        const int kl = (int)fdiv(l, p.fd_cg), cl = l - kl * CG;
+        return (cl < ncg && kl < nkb) ? p.tmp[(((size_t)b * p.c + c0 + cl) * p.wh + kx0 + kl) * H + y]
+                                      : make_float2(0.f, 0.f);
+      },
+      [&](int t, float2 v) {
+        const int l = (int)fdiv(t, p.fd_h);
+        buf[l * ls + t - l * H] = v;
+      });
   __syncthreads();
-  const float2* L = transform_lines(buf, tmp, nl, ls, H, p.rad_h, tw, direction(p.log2h, false));
+  const float2* L = transform_lines(buf, tmp, nl, ls, p.rad_h, tw, direction(p.log2h, false));
   // spectrum [b][ky][kx][2c + part], channel fastest
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.spec);
   const int C2 = 2 * p.c;
   for (int t = threadIdx.x; t < nl * H; t += blockDim.x) {
-    const int cl = t % ncg, r = t / ncg, kl = r % nkb, ky = r / nkb;
-    const float2 v = L[(kl * ncg + cl) * ls + ky];
+    const int r = (int)fdiv(t, p.fd_cg), cl = t - r * CG;
+    const int ky = (int)fdiv(r, p.fd_kb), kl = r - ky * p.kb;
+    if (cl >= ncg || kl >= nkb) continue;
+    const float2 v = L[(kl * CG + cl) * ls + ky];
     uint32_t hi, lo;
     split_pair(v.x * p.scale, v.y * p.scale, hi, lo);
     const size_t off = (((size_t)b * H + ky) * p.wh + kx0 + kl) * C2 + 2 * (c0 + cl);
@@ -280,25 +347,36 @@ __global__ void __launch_bounds__(kThreads) k_cols_fwd(const FftParams p) {
 __global__ void __launch_bounds__(kThreads) k_cols_inv(const FftParams p) {
   extern __shared__ __align__(16) float2 sm[];
   const int b = blockIdx.z, c0 = blockIdx.y * p.cg, kx0 = blockIdx.x * p.kb;
-  const int H = p.h, ls = H + 1;
-  const int ncg = min(p.cg, p.c - c0), nkb = min(p.kb, p.wh - kx0), nl = ncg * nkb;
+  const int H = p.h, ls = H + 1, CG = p.cg, nl = CG * p.kb;
+  const int ncg = min(CG, p.c - c0), nkb = min(p.kb, p.wh - kx0);
   float2* tw = sm;
   float2* buf = tw + H;
-  float2* tmp = buf + p.cg * p.kb * ls;
+  float2* tmp = buf + nl * ls;
   load_tw(tw, p.tw_h, H);
   const int C2 = 2 * p.c;
-  for (int t = threadIdx.x; t < nl * H; t += blockDim.x) {
-    const int cl = t % ncg, r = t / ncg, kl = r % nkb, ky = r / nkb;
-    const float2 v = *reinterpret_cast<const float2*>(p.fu + (((size_t)b * H + ky) * p.wh + kx0 + kl) * C2 +
-                                                      2 * (c0 + cl));
-    buf[(kl * ncg + cl) * ls + ky] = v;
-  }
+  batched<8>(
+      nl * H,
+      [&](int t) {
+        const int r = (int)fdiv(t, p.fd_cg), cl = t - r * CG;
+        const int ky = (int)fdiv(r, p.fd_kb), kl = r - ky * p.kb;
+        float2 v = make_float2(0.f, 0.f);
+        if (cl < ncg && kl < nkb)
+          v = *reinterpret_cast<const float2*>(p.fu + (((size_t)b * H + ky) * p.wh + kx0 + kl) * C2 + 2 * (c0 + cl));
+        return v;
+      },
+      [&](int t, float2 v) {
+        const int r = (int)fdiv(t, p.fd_cg), cl = t - r * CG;
+        const int ky = (int)fdiv(r, p.fd_kb), kl = r - ky * p.kb;
+        buf[(kl * CG + cl) * ls + ky] = v;
+      });
   __syncthreads();
-  const float2* L = transform_lines(buf, tmp, nl, ls, H, p.rad_h, tw, direction(p.log2h, true));
+  const float2* L = transform_lines(buf, tmp, nl, ls, p.rad_h, tw, direction(p.log2h, true));
   // T[b][y][kx][c], channel fastest
   for (int t = threadIdx.x; t < nl * H; t += blockDim.x) {
-    const int cl = t % ncg, r = t / ncg, kl = r % nkb, y = r / nkb;
-    p.tmp[(((size_t)b * H + y) * p.wh + kx0 + kl) * p.c + c0 + cl] = L[(kl * ncg + cl) * ls + y];
+    const int r = (int)fdiv(t, p.fd_cg), cl = t - r * CG;
+    const int y = (int)fdiv(r, p.fd_kb), kl = r - y * p.kb;
+    if (cl >= ncg || kl >= nkb) continue;
+    p.tmp[(((size_t)b * H + y) * p.wh + kx0 + kl) * p.c + c0 + cl] = L[(kl * CG + cl) * ls + y];
   }
 }
 
@@ -306,47 +384,88 @@ __global__ void __launch_bounds__(kThreads) k_cols_inv(const FftParams p) {
 __global__ void __launch_bounds__(kThreads) k_rows_inv(const FftParams p) {
   extern __shared__ __align__(16) float2 sm[];
   const int b = blockIdx.z, c0 = blockIdx.y * p.cg, y0 = blockIdx.x * 2 * p.rpi;
-  const int W = p.w, ls = W + 1, fs = W + 1;
-  const int ncg = min(p.cg, p.c - c0), nrows = min(2 * p.rpi, p.h - y0), npair = (nrows + 1) >> 1;
-  const int nl = npair * ncg;
+  const int W = p.w, ls = W + 1, fs = W + 1, CG = p.cg, nl = p.rpi * CG;
+  const int ncg = min(CG, p.c - c0), nrows = min(2 * p.rpi, p.h - y0);
   float2* tw = sm;
   float2* buf = tw + W;
-  float2* tmp = buf + p.rpi * p.cg * ls;
+  float2* tmp = buf + nl * ls;
   load_tw(tw, p.tw_w, W);
   // Hermitian completion of each row's bins; line (pair, channel) = row a + i row b
-  for (int t = threadIdx.x; t < nl * W; t += blockDim.x) {
-    const int cl = t % ncg, r = t / ncg, k = r % W, pr = r / W;
-    const int ya = y0 + 2 * pr, yb = ya + 1;
-    const bool mirror = k >= p.wh;
-    const int kk = mirror ? W - k : k;
-    const float2* Ta = p.tmp + (((size_t)b * p.h + ya) * p.wh + kk) * p.c + c0 + cl;
-    float2 a = Ta[0];
-    float2 bb = yb < y0 + nrows ? Ta[(size_t)p.wh * p.c] : make_float2(0.f, 0.f);
-    if (k == 0 || 2 * k == W) {
-      a.y = 0.f;
-      bb.y = 0.f;
-    }
-    if (mirror) {
-      a.y = -a.y;
-      bb.y = -bb.y;
-    }
-    buf[(pr * ncg + cl) * ls + k] = make_float2(a.x - bb.y, a.y + bb.x);
-  }
+  batched<4>(
+      nl * W,
+      [&](int t) {
+        const int r = (int)fdiv(t, p.fd_cg), cl = t - r * CG;
+        const int pr = (int)fdiv(r, p.fd_w), k = r - pr * W;
+        const int ya = 2 * pr, yb = ya + 1;
+        float2 a = make_float2(0.f, 0.f), bb = make_float2(0.f, 0.f);
+        if (cl < ncg && ya < nrows) {
+          const bool mirror = k >= p.wh;
+          const int kk = mirror ? W - k : k;
+          const float2* Ta = p.tmp + (((size_t)b * p.h + y0 + ya) * p.wh + kk) * p.c + c0 + cl;
+          a = Ta[0];
+          if (yb < nrows) bb = Ta[(size_t)p.wh * p.c];
+          if (k == 0 || 2 * k == W) {
+            a.y = 0.f;
+            bb.y = 0.f;
+          }
+          if (mirror) {
+            a.y = -a.y;
+            bb.y = -bb.y;
+          }
+        }
+        return make_float2(a.x - bb.y, a.y + bb.x);
+      },
+      [&](int t, float2 v) {
+        const int r = (int)fdiv(t, p.fd_cg), cl = t - r * CG;
+        const int pr = (int)fdiv(r, p.fd_w), k = r - pr * W;
+        buf[(pr * CG + cl) * ls + k] = v;
+      });
   __syncthreads();
-  const float2* L = transform_lines(buf, tmp, nl, ls, W, p.rad_w, tw, direction(p.log2w, true));
+  const float2* L = transform_lines(buf, tmp, nl, ls, p.rad_w, tw, direction(p.log2w, true));
   // feat rows of this tile, coalesced along x, into the buffer the result is not in
   float* fe = reinterpret_cast<float*>(L == buf ? tmp : buf);  // [row][channel][x]
-  for (int t = threadIdx.x; t < nrows * ncg * W; t += blockDim.x) {
-    const int x = t % W, r = t / W, cl = r % ncg, row = r / ncg;
-    fe[(row * ncg + cl) * fs + x] = p.feat[(((size_t)b * p.c + c0 + cl) * p.h + y0 + row) * W + x];
+  if ((W & 3) == 0 && aligned16(p.feat)) {
+    const int W4 = W >> 2;
+    batched<4>(
+        2 * nl * W4,
+        [&](int t) {
+          const int r = t / W4, x = (t - r * W4) * 4;
+          const int row = (int)fdiv(r, p.fd_cg), cl = r - row * CG;
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (row < nrows && cl < ncg)
+            v = *reinterpret_cast<const float4*>(p.feat + (((size_t)b * p.c + c0 + cl) * p.h + y0 + row) * W + x);
+          return v;
+        },
+        [&](int t, const float4& v) {
+          const int r = t / W4, x = (t - r * W4) * 4;
+          float* d = fe + r * fs + x;  // r = row * CG + cl
+          d[0] = v.x;
+          d[1] = v.y;
+          d[2] = v.z;
+          d[3] = v.w;
+        });
+  } else {
+    batched<8>(
+        2 * nl * W,
+        [&](int t) {
+          const int r = (int)fdiv(t, p.fd_w), x = t - r * W;
+          const int row = (int)fdiv(r, p.fd_cg), cl = r - row * CG;
+          return (row < nrows && cl < ncg) ? p.feat[(((size_t)b * p.c + c0 + cl) * p.h + y0 + row) * W + x] : 0.f;
+        },
+        [&](int t, float v) {
+          const int r = (int)fdiv(t, p.fd_w);
+          fe[r * fs + t - r * W] = v;
+        });
   }
   __syncthreads();
   // S [b][y][x][c] = feat + scale * row, channel fastest
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.s_out);
-  for (int t = threadIdx.x; t < nrows * W * ncg; t += blockDim.x) {
-    const int cl = t % ncg, r = t / ncg, x = r % W, row = r / W;
-    const float2 v = L[((row >> 1) * ncg + cl) * ls + x];
-    const float s = ((row & 1) ? v.y : v.x) * p.scale + fe[(row * ncg + cl) * fs + x];
+  for (int t = threadIdx.x; t < 2 * nl * W; t += blockDim.x) {
+    const int r = (int)fdiv(t, p.fd_cg), cl = t - r * CG;
+    const int row = (int)fdiv(r, p.fd_w), x = r - row * W;
+    if (row >= nrows || cl >= ncg) continue;
+    const float2 v = L[((row >> 1) * CG + cl) * ls + x];
+    const float s = ((row & 1) ? v.y : v.x) * p.scale + fe[(row * CG + cl) * fs + x];
     const __nv_bfloat16 hs = __float2bfloat16_rn(s);
     const size_t o = (((size_t)b * p.h + y0 + row) * W + x) * p.c + c0 + cl;
     out[o] = hs;
@@ -374,7 +493,23 @@ size_t fft_smem_bytes(const FftParams& p, int pass) {
 // a two, then threes, fives and any other prime factors.
 Radices fft_radices(int n) {
   Radices r{};
-  auto push = [&r](int f) { r.r[r.n++] = f; };
+  int cnt = 0, ns = 1;
+  const int len = n;
+  r.n = n;
+  r.len = make_fastdiv((unsigned)n);
+  auto push = [&](int f) {
+    if (cnt == 12) {  // more stages than a plan holds: reported as unsupported
+      r.n = 0;
+      return;
+    }
+    FftStage& s = r.st[cnt++];
+    s.r = f;
+    s.m = make_fastdiv((unsigned)(len / f));
+    s.ns = make_fastdiv((unsigned)ns);
+    s.rr = make_fastdiv((unsigned)f);
+    s.nsr = make_fastdiv((unsigned)(ns * f));
+    ns *= f;
+  };
   int k = 0;
   while (n % 2 == 0) {
     n /= 2;
@@ -386,8 +521,10 @@ Radices fft_radices(int n) {
   }
   if (k == 2) push(4);
   if (k == 1) {
-    if (r.n > 0) {
-      r.r[r.n - 1] = 4;
+    if (cnt > 0) {  // ... x 8 x 2 -> ... x 4 x 4
+      ns /= 8;
+      cnt--;
+      push(4);
       push(4);
     } else {
       push(2);
@@ -406,13 +543,20 @@ bool fft_tiles(FftParams& p, size_t max_smem) {
   const int w = std::max(1, p.w), h = std::max(1, p.h), pairs = (h + 1) / 2;
   p.rad_h = fft_radices(h);
   p.rad_w = fft_radices(w);
+  if (p.rad_h.n == 0 || p.rad_w.n == 0) return false;
+  p.fd_w = make_fastdiv((unsigned)w);
+  p.fd_h = make_fastdiv((unsigned)h);
   p.rp = std::max(1, std::min(kElems / w, pairs));
   for (p.cg = std::min(16, p.c); p.cg >= 1; p.cg /= 2) {
     p.kb = std::max(1, std::min(kElems / (p.cg * h), p.wh));
     p.rpi = std::max(1, std::min(kElems / (p.cg * w), pairs));
     if (fft_smem_bytes(p, 1) <= max_smem && fft_smem_bytes(p, 2) <= max_smem) break;
   }
-  return p.cg >= 1 && fft_smem_bytes(p, 0) <= max_smem;
+  if (p.cg < 1) return false;
+  p.fd_cg = make_fastdiv((unsigned)p.cg);
+  p.fd_kb = make_fastdiv((unsigned)p.kb);
+  p.fd_rows = make_fastdiv((unsigned)(2 * p.rp));
+  return fft_smem_bytes(p, 0) <= max_smem;
 }
 
 size_t fft_tmp_elems(const FftParams& p) { return (size_t)p.batch * p.c * p.wh * p.h; }

@@ -7,10 +7,36 @@
 
 namespace lama {
 
-// Stockham stage radices of one line length (product = the length).
+// Division by a divisor fixed at plan time (Granlund & Montgomery, "Division
+// by invariant integers using multiplication", 1994, round-up variant):
+// x / d = (umulhi(x, m) + x) >> s for 0 <= x < 2^31.
+struct FastDiv {
+  unsigned d, m, s;
+};
+
+inline FastDiv make_fastdiv(unsigned d) {
+  FastDiv f{d, 0, 0};
+  while ((1u << f.s) < d) f.s++;
+  f.m = (unsigned)((((unsigned long long)1 << 32) * (((unsigned long long)1 << f.s) - d)) / d + 1);
+  return f;
+}
+
+#ifdef __CUDACC__
+__device__ __forceinline__ unsigned fdiv(unsigned x, const FastDiv& f) { return (__umulhi(x, f.m) + x) >> f.s; }
+#endif
+
+// One Stockham stage: radix R, Ns = product of the radices before it, and
+// the divisors its index arithmetic needs (m = n / R).
+struct FftStage {
+  int r;
+  FastDiv m, ns, rr, nsr;
+};
+
+// The stages of one line length n (product of the radices = n).
 struct Radices {
   int n;
-  int r[16];
+  FastDiv len;
+  FftStage st[12];
 };
 
 struct FftParams {
@@ -31,7 +57,8 @@ struct FftParams {
   void* s_out;             // irfft2 out: split bf16 [2][B][h][w][c] = feat + irfft2(fu)
   long long s_part;
   float2* tmp;             // fft.cu: intermediate, fft_tmp_elems(p) complex values
-  Radices rad_h, rad_w;    // fft.cu: stage radices of the column / row transforms
+  Radices rad_h, rad_w;    // fft.cu: stages of the column / row transforms
+  FastDiv fd_w, fd_h, fd_cg, fd_kb, fd_rows;  // fft.cu: w, h, cg, kb, 2 * rp
 };
 
 // Two-pass kernels for any plane size (fft.cu).  fft_tiles fills cg/kb/rp/rpi
