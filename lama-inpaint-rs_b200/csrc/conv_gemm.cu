@@ -40,8 +40,15 @@ __host__ __device__ constexpr int stages_for(int bn) {
 // Extra shared memory of the shifted-sum epilogue (OUT_SHIFT7_NCHW):
 // two 128 x 33 fp32 staging tiles.
 constexpr int SHIFT_LD = 33;
+// Tile widths whose split outputs can leave through TMA stores: each of the
+// 8 epilogue warps stages 32 pixels x 32 channels (hi and lo, 2 KB each) at
+// STAGING_OFF past the pipeline stages.
+__host__ __device__ constexpr bool tma_store_bn(int bn) { return bn == 64 || bn == 128 || bn == 192; }
+constexpr uint32_t STAGING_OFF = 1024;
+constexpr uint32_t STAGING_WARP = 4096;
 __host__ __device__ constexpr uint32_t extra_smem(int bn) {
-  return bn == 32 ? 2u * 128u * SHIFT_LD * 4u : bn == 256 ? 8u * 32u * SHIFT_LD * 4u : 0u;
+  return bn == 32 ? 2u * 128u * SHIFT_LD * 4u
+                  : bn == 256 ? 8u * 32u * SHIFT_LD * 4u : tma_store_bn(bn) ? STAGING_OFF - 256u + 8u * STAGING_WARP : 0u;
 }
 __host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 2 * A_PART + 2u * (uint32_t)bn * 128u; }
 __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
@@ -114,12 +121,10 @@ __device__ __forceinline__ void store_split(const GemmParams& p, int b, int oy, 
     }
 }
 
-// Residual, sigmoid and the store of CH channels [C.n0, C.n0 + CH) of one
-// output pixel whose values already carry the per-channel affine and ReLU.
+// Residual and sigmoid of CH channels starting at absolute channel n of one
+// output pixel.
 template <int CH>
-__device__ __forceinline__ void store_channels(const GemmParams& p, const GemmClass& C, int b, int oy, int ox,
-                                               float* v, int nloc = 0) {
-  const int n = C.n0 + nloc;
+__device__ __forceinline__ void finish_channels(const GemmParams& p, int b, int oy, int ox, int n, float* v) {
   if (p.skip) {
     const int hp = p.out_h + 2 * p.out_halo, wp = p.out_w + 2 * p.out_halo;
     long long off = (((long long)b * hp + oy + p.out_halo) * wp + ox + p.out_halo) * p.out_c + n;
@@ -143,6 +148,15 @@ __device__ __forceinline__ void store_channels(const GemmParams& p, const GemmCl
       v[k] = 1.0f / (1.0f + e);
     }
   }
+}
+
+// Residual, sigmoid and the store of CH channels [C.n0, C.n0 + CH) of one
+// output pixel whose values already carry the per-channel affine and ReLU.
+template <int CH>
+__device__ __forceinline__ void store_channels(const GemmParams& p, const GemmClass& C, int b, int oy, int ox,
+                                               float* v, int nloc = 0) {
+  const int n = C.n0 + nloc;
+  finish_channels<CH>(p, b, oy, ox, n, v);
   if (p.out_kind == OUT_SPLIT) {
     store_split<CH>(p, b, oy, ox, n, v);
   } else if (p.out_kind == OUT_F32_NHWC) {
@@ -157,6 +171,78 @@ __device__ __forceinline__ void store_channels(const GemmParams& p, const GemmCl
     for (int k = 0; k < CH; k++)
       if (nloc + k < C.nvalid)
         o[(((long long)b * p.out_c + n + k) * p.out_h + oy) * p.out_w + ox] = v[k];
+  }
+}
+
+// The reflected halo copies of one output pixel (every target but the
+// interior one), split bf16.
+__device__ __forceinline__ void store_split_halo(const GemmParams& p, int b, int oy, int ox, int n,
+                                                 const uint32_t* hi, const uint32_t* lo) {
+  int ty[7], tx[7];
+  const int ny = halo_targets(oy, p.out_h, p.out_halo, p.out_reflect, ty);
+  const int nx = halo_targets(ox, p.out_w, p.out_halo, p.out_reflect, tx);
+  if (ny == 1 && nx == 1) return;
+  const int hp = p.out_h + 2 * p.out_halo, wp = p.out_w + 2 * p.out_halo;
+  __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(p.out);
+  for (int a = 0; a < ny; a++)
+    for (int c = 0; c < nx; c++) {
+      if (a == 0 && c == 0) continue;
+      long long off = (((long long)b * hp + ty[a]) * wp + tx[c]) * p.out_c + n;
+      uint4* dh = reinterpret_cast<uint4*>(base + off);
+      uint4* dl = reinterpret_cast<uint4*>(base + p.out_part + off);
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        dh[k] = make_uint4(hi[4 * k], hi[4 * k + 1], hi[4 * k + 2], hi[4 * k + 3]);
+        dl[k] = make_uint4(lo[4 * k], lo[4 * k + 1], lo[4 * k + 2], lo[4 * k + 3]);
+      }
+    }
+}
+
+// Split store of one warp's 32 pixels x 32 channels through the TMA unit: the
+// lane's pixel row goes to the warp's staging tile (64-byte swizzle, the
+// layout omap's box expects), one lane issues the hi and lo box stores, and
+// border lanes add their reflected halo copies with ordinary stores.  The
+// previous chunk's stores must have read the staging tile first.
+__device__ __forceinline__ void store_split_tma(const GemmParams& p, uint8_t* stage, int lane, bool valid, int b,
+                                                int oy, int ox, int n, int box_x, int box_y, const float* v) {
+  uint32_t hi[16], lo[16];
+#pragma unroll
+  for (int k = 0; k < 16; k++) split_pair(v[2 * k], v[2 * k + 1], hi[k], lo[k]);
+  if (lane == 0) bulk_wait_read0();
+  __syncwarp();
+  const int sw = (lane >> 1) & 3;
+  uint4* sh = reinterpret_cast<uint4*>(stage + lane * 64);
+  uint4* sl = reinterpret_cast<uint4*>(stage + 2048 + lane * 64);
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    sh[k ^ sw] = make_uint4(hi[4 * k], hi[4 * k + 1], hi[4 * k + 2], hi[4 * k + 3]);
+    sl[k ^ sw] = make_uint4(lo[4 * k], lo[4 * k + 1], lo[4 * k + 2], lo[4 * k + 3]);
+  }
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_5d(&p.omap, smem_u32(stage), n, box_x, box_y, b, 0);
+    tma_store_5d(&p.omap, smem_u32(stage + 2048), n, box_x, box_y, b, 1);
+    bulk_commit();
+  }
+  if (valid && p.out_halo && p.out_reflect) store_split_halo(p, b, oy, ox, n, hi, lo);
+}
+
+template <int CH>
+__device__ __forceinline__ void affine_relu(const GemmParams& p, const GemmClass& C, int nloc, float* v) {
+  const int n = C.n0 + nloc;
+#pragma unroll
+  for (int k = 0; k < CH; k++) {
+    int nn = n + k;
+    float s = 1.f, t = 0.f;
+    if (nloc + k < C.nvalid) {
+      s = __ldg(p.scale + nn);
+      t = __ldg(p.shift + nn);
+    }
+    float x = v[k] * s;
+    x = x + t;
+    if (p.relu) x = x > 0.f ? x : 0.f;
+    v[k] = x;
   }
 }
 
@@ -410,6 +496,29 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           continue;
         }
       }
+      if constexpr (tma_store_bn(BN)) {
+        if (p.ostore) {
+          // box origin: the warp's first pixel (32 consecutive M rows)
+          const int m0 = quarter * 32;
+          const int box_x = ti.j0 + m0 % p.bw + C.ox_add + p.out_halo;
+          const int box_y = ti.i0 + m0 / p.bw + C.oy_add + p.out_halo;
+          uint8_t* stage = smem + STAGES * STAGE + STAGING_OFF + ew * STAGING_WARP;
+#pragma unroll 1
+          for (int ch = half; ch < BN / 32; ch += 2) {
+            float v[32];
+            tmem_ld32(trow + ch * 32, v);
+            tmem_wait_ld();
+            const int nloc = ti.nt * BN + ch * 32;
+            if (nloc >= C.nvalid) continue;
+            affine_relu<32>(p, C, nloc, v);
+            if (valid) finish_channels<32>(p, ti.b, oy, ox, C.n0 + nloc, v);
+            store_split_tma(p, stage, lane, valid, ti.b, oy, ox, C.n0 + nloc, box_x, box_y, v);
+          }
+          tc_fence_before();
+          mbar_arrive(tempty_bar(acc));
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int ch = half; ch < BN / CH; ch += 2) {
         float v[CH];
@@ -421,6 +530,9 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       }
       tc_fence_before();
       mbar_arrive(tempty_bar(acc));
+    }
+    if constexpr (tma_store_bn(BN)) {
+      if (p.ostore && lane == 0) bulk_wait0();
     }
   }
 

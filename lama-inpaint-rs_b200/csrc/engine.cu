@@ -149,6 +149,26 @@ CUtensorMap act_map(const Act& a, int cb, int bw, int bh, int stride, bool inter
   return m;
 }
 
+// Split output addressed from its padded origin with extents W + halo, H + halo:
+// interior boxes start at (x + halo, y + halo) and are clipped at the far
+// edges, so they never touch the trailing halo (written by reflection).
+CUtensorMap out_map(void* p, long long part, int B, int C, int H, int W, int halo, int bw) {
+  CUtensorMap m;
+  const int hp = H + 2 * halo, wp = W + 2 * halo;
+  cuuint64_t dims[5] = {(cuuint64_t)C, (cuuint64_t)(W + halo), (cuuint64_t)(H + halo), (cuuint64_t)B, 2};
+  cuuint64_t strides[4] = {(cuuint64_t)C * 2, (cuuint64_t)wp * C * 2, (cuuint64_t)hp * wp * C * 2,
+                           (cuuint64_t)part * 2};
+  const int bx = std::min(bw, 32);
+  cuuint32_t box[5] = {32, (cuuint32_t)bx, (cuuint32_t)(32 / bx), 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, p, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw EngineError{LAMA_ECUDA, "cuTensorMapEncodeTiled (output) failed: " + std::to_string((int)r)};
+  return m;
+}
+
 // ------------------------------------------------------------------ weights
 struct WClass {
   int n = 0, npad = 0, k = 0;
@@ -664,6 +684,15 @@ struct Builder {
     p.out_reflect = o.reflect;
     p.skip = o.skip;
     p.err = e.d_err;
+    // split outputs of pixel-major tiles with dense placement leave through TMA stores
+    bool dense = true;
+    for (auto& c : classes) dense = dense && c.oy_mul == 1 && c.ox_mul == 1;
+    if (o.kind == OUT_SPLIT && !swap && (bn == 64 || bn == 128 || bn == 192) && o.c % 32 == 0 && dense &&
+        p.step_x == bw && (bw >= 32 ? bw % 32 == 0 : 32 % bw == 0)) {
+      p.omap = out_map(o.p, o.part, B, o.c, o.h, o.w, o.halo, bw);
+      p.ostore = 1;
+      p.obox_w = std::min(bw, 32);
+    }
     op.grid = std::min(p.total_tiles, e.sms);
     op.out_ptr = o.p;
     op.out_split = o.kind == OUT_SPLIT;

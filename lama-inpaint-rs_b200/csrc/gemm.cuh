@@ -65,6 +65,12 @@ struct GemmClass {
 struct GemmParams {
   CUtensorMap amap[GEMM_MAX_AMAPS];
   CUtensorMap bmap[GEMM_MAX_CLASSES];
+  // ostore = 1: split outputs leave through the TMA unit.  omap addresses the
+  // output's interior plus its leading halo, (C, W + h, H + h, B, part) from
+  // the padded origin, so boxes are clipped at the interior's far edges; a
+  // box is 32 channels x (obox_w x 32 / obox_w) pixels, 64-byte swizzled.
+  CUtensorMap omap;
+  int ostore, obox_w;
   GemmClass cls[GEMM_MAX_CLASSES];
   int nclass;
   int swap;                   // 1: M = 128 output channels, N = BN pixels (see conv_gemm.cu)
