@@ -198,6 +198,32 @@ __device__ __forceinline__ void store_split_halo(const GemmParams& p, int b, int
     }
 }
 
+// fp32 store of one warp's 32 pixels x 32 channels through the TMA unit
+// (ostore 2: NCHW, the staging tile is [channel][pixel]; ostore 3: NHWC,
+// [pixel][channel] with the 128-byte swizzle).
+__device__ __forceinline__ void store_f32_tma(const GemmParams& p, uint8_t* stage, int lane, int b, int n, int box_x,
+                                              int box_y, const float* v) {
+  if (lane == 0) bulk_wait_read0();
+  __syncwarp();
+  if (p.ostore == 2) {
+    float* st = reinterpret_cast<float*>(stage);
+#pragma unroll
+    for (int k = 0; k < 32; k++) st[k * 32 + lane] = v[k];
+  } else {
+    uint4* st = reinterpret_cast<uint4*>(stage + lane * 128);
+#pragma unroll
+    for (int k = 0; k < 8; k++) st[k ^ (lane & 7)] = make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                                                                 __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
+  }
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (p.ostore == 2) tma_store_4d(&p.omap, smem_u32(stage), box_x, box_y, n, b);
+    else tma_store_4d(&p.omap, smem_u32(stage), n, box_x, box_y, b);
+    bulk_commit();
+  }
+}
+
 // Split store of one warp's 32 pixels x 32 channels through the TMA unit: the
 // lane's pixel row goes to the warp's staging tile (64-byte swizzle, the
 // layout omap's box expects), one lane issues the hi and lo box stores, and
@@ -512,7 +538,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
             if (nloc >= C.nvalid) continue;
             affine_relu<32>(p, C, nloc, v);
             if (valid) finish_channels<32>(p, ti.b, oy, ox, C.n0 + nloc, v);
-            store_split_tma(p, stage, lane, valid, ti.b, oy, ox, C.n0 + nloc, box_x, box_y, v);
+            if (p.ostore == 1) store_split_tma(p, stage, lane, valid, ti.b, oy, ox, C.n0 + nloc, box_x, box_y, v);
+            else store_f32_tma(p, stage, lane, ti.b, C.n0 + nloc, box_x, box_y, v);
           }
           tc_fence_before();
           mbar_arrive(tempty_bar(acc));

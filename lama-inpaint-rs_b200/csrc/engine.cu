@@ -169,6 +169,39 @@ CUtensorMap out_map(void* p, long long part, int B, int C, int H, int W, int hal
   return m;
 }
 
+// fp32 output, NCHW (W, H, C, B) or NHWC (C, W, H, B), boxes of 32 channels x
+// 32 pixels (min(bw, 32) wide).
+CUtensorMap out_map_f32(void* p, bool nchw, int B, int C, int H, int W, int bw) {
+  CUtensorMap m;
+  const int bx = std::min(bw, 32);
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t box[4];
+  if (nchw) {
+    dims[0] = (cuuint64_t)W; dims[1] = (cuuint64_t)H; dims[2] = (cuuint64_t)C; dims[3] = (cuuint64_t)B;
+    strides[0] = (cuuint64_t)W * 4; strides[1] = (cuuint64_t)H * W * 4; strides[2] = (cuuint64_t)C * H * W * 4;
+    box[0] = (cuuint32_t)bx; box[1] = (cuuint32_t)(32 / bx); box[2] = 32; box[3] = 1;
+  } else {
+    dims[0] = (cuuint64_t)C; dims[1] = (cuuint64_t)W; dims[2] = (cuuint64_t)H; dims[3] = (cuuint64_t)B;
+    strides[0] = (cuuint64_t)C * 4; strides[1] = (cuuint64_t)W * C * 4; strides[2] = (cuuint64_t)H * W * C * 4;
+    box[0] = 32; box[1] = (cuuint32_t)bx; box[2] = (cuuint32_t)(32 / bx); box[3] = 1;
+  }
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           nchw ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::string d = " dims";
+    for (int i = 0; i < 4; i++) d += " " + std::to_string((unsigned long long)dims[i]);
+    d += " strides";
+    for (int i = 0; i < 3; i++) d += " " + std::to_string((unsigned long long)strides[i]);
+    d += " box";
+    for (int i = 0; i < 4; i++) d += " " + std::to_string((unsigned)box[i]);
+    throw EngineError{LAMA_ECUDA, "cuTensorMapEncodeTiled (fp32 output) failed: " + std::to_string((int)r) + d};
+  }
+  return m;
+}
+
 // ------------------------------------------------------------------ weights
 struct WClass {
   int n = 0, npad = 0, k = 0;
@@ -685,12 +718,23 @@ struct Builder {
     p.skip = o.skip;
     p.err = e.d_err;
     // split outputs of pixel-major tiles with dense placement leave through TMA stores
-    bool dense = true;
-    for (auto& c : classes) dense = dense && c.oy_mul == 1 && c.ox_mul == 1;
-    if (o.kind == OUT_SPLIT && !swap && (bn == 64 || bn == 128 || bn == 192) && o.c % 32 == 0 && dense &&
-        p.step_x == bw && (bw >= 32 ? bw % 32 == 0 : 32 % bw == 0)) {
-      p.omap = out_map(o.p, o.part, B, o.c, o.h, o.w, o.halo, bw);
-      p.ostore = 1;
+    // (TMA boxes need a 16-byte aligned innermost coordinate: channel starts on
+    // multiples of 32; for NCHW, whose innermost coordinate is x, tile
+    // columns on multiples of 4)
+    bool dense = true, x4 = bw % 4 == 0 && o.w % 4 == 0;  // NCHW rows must also be 16-byte strides
+    for (auto& c : classes) {
+      dense = dense && c.oy_mul == 1 && c.ox_mul == 1 && c.n0 % 32 == 0;
+      x4 = x4 && c.ox_add % 4 == 0;
+    }
+    if (!swap && (bn == 64 || bn == 128 || bn == 192) && o.c % 32 == 0 && dense && p.step_x == bw &&
+        (bw >= 32 ? bw % 32 == 0 : 32 % bw == 0)) {
+      if (o.kind == OUT_SPLIT) {
+        p.omap = out_map(o.p, o.part, B, o.c, o.h, o.w, o.halo, bw);
+        p.ostore = 1;
+      } else if ((o.kind == OUT_F32_NHWC || (o.kind == OUT_F32_NCHW && x4)) && o.halo == 0) {
+        p.omap = out_map_f32(o.p, o.kind == OUT_F32_NCHW, B, o.c, o.h, o.w, bw);
+        p.ostore = o.kind == OUT_F32_NCHW ? 2 : 3;
+      }
       p.obox_w = std::min(bw, 32);
     }
     op.grid = std::min(p.total_tiles, e.sms);

@@ -65,10 +65,12 @@ struct GemmClass {
 struct GemmParams {
   CUtensorMap amap[GEMM_MAX_AMAPS];
   CUtensorMap bmap[GEMM_MAX_CLASSES];
-  // ostore = 1: split outputs leave through the TMA unit.  omap addresses the
-  // output's interior plus its leading halo, (C, W + h, H + h, B, part) from
-  // the padded origin, so boxes are clipped at the interior's far edges; a
-  // box is 32 channels x (obox_w x 32 / obox_w) pixels, 64-byte swizzled.
+  // ostore != 0: the output leaves through TMA tensor stores of one box per
+  // epilogue warp and 32-channel chunk (32 channels x obox_w x 32 / obox_w
+  // pixels).  1 = split: omap is (C, W + h, H + h, B, part) from the padded
+  // origin (boxes clip at the interior's far edges, the trailing halo is
+  // written by reflection), 64-byte swizzled; 2 = fp32 NCHW: (W, H, C, B);
+  // 3 = fp32 NHWC: (C, W, H, B), 128-byte swizzled.
   CUtensorMap omap;
   int ostore, obox_w;
   GemmClass cls[GEMM_MAX_CLASSES];
