@@ -92,11 +92,14 @@ int lama_resblocks_device(lama_engine* e, const float* d_local_in, const float* 
                           int w, int nblocks, float* d_local_out, float* d_global_out);
 
 /* Tile policy of the convolution GEMMs for plans built after this call
- * (cached plans are dropped): LAMA_TILING_AUTO picks per launch,
+ * (cached plans are dropped): LAMA_TILING_AUTO uses pixel-major tiles,
+ * shared by CTA pairs when a launch has at least two M tiles per SM,
  * LAMA_TILING_SWAPPED uses channel-major tiles (M = 128 output channels,
- * N = 256 pixels) wherever they apply, LAMA_TILING_PIXEL never does.  All
- * policies compute the same function; tests use this to cover both kernels. */
-enum { LAMA_TILING_AUTO = 0, LAMA_TILING_SWAPPED = 1, LAMA_TILING_PIXEL = 2 };
+ * N = 256 pixels) wherever they apply, LAMA_TILING_PIXEL uses single-CTA
+ * pixel-major tiles only, LAMA_TILING_PAIRED uses pixel-major tiles shared by
+ * CTA pairs (256 pixels x 128 channels over two SMs) wherever they apply.  All
+ * policies compute the same function; tests use this to cover each kernel. */
+enum { LAMA_TILING_AUTO = 0, LAMA_TILING_SWAPPED = 1, LAMA_TILING_PIXEL = 2, LAMA_TILING_PAIRED = 3 };
 int lama_set_tiling(lama_engine* e, int policy);
 
 /* Spectral-transform kernels for plans built after this call (cached plans

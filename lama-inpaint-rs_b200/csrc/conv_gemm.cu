@@ -57,9 +57,12 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
 
 struct TileInfo {
   int cls, nt, b, i0, j0;
+  bool dummy;  // CTA-pair tile past the class's last M tile (loads zeros, stores nothing)
 };
 
-__device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
+// Tile t of the launch.  With CTA pairs (p.pair) t counts pair tiles: the
+// pair's two CTAs take M tiles 2m and 2m + 1 (rank) of the same N tile.
+__device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t, int rank = 0) {
   TileInfo ti;
   int c = 0;
   while (c + 1 < p.nclass && t >= p.cls[c + 1].tile0) c++;
@@ -68,6 +71,8 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
   ti.cls = c;
   ti.nt = lt % C.ntiles_n;
   int mt = lt / C.ntiles_n;
+  if (p.pair) mt = 2 * mt + rank;
+  ti.dummy = mt >= p.m_tiles;
   int per_img = p.tiles_y * p.tiles_x;
   ti.b = mt / per_img;
   int r = mt - ti.b * per_img;
@@ -340,14 +345,24 @@ __device__ __forceinline__ void epilogue_swapped(const GemmParams& p, const Gemm
 //               more MACs per staged byte when the output has >= 128 channels
 //               (BN = 256: 65 MAC/B instead of 48 at BN = 128).  The epilogue then
 //               holds one output channel per thread and walks the tile's pixels.
-template <int BN, bool SWAP>
+//
+// PAIR: a cluster of two CTAs computes 256 x BN tiles with cta_group::2 MMAs.
+// Each CTA stages its own 128 A rows and BN/2 B rows (so a stage carries a
+// quarter less than a single-CTA 128 x BN stage for the same MMA work, and the
+// pipeline gets one more stage); the even CTA's barriers count both CTAs' TMA
+// bytes and both epilogues' releases, its MMA warp issues for the pair, and
+// commits arrive on both CTAs' barriers.  Each CTA's epilogue drains its own
+// TMEM (its 128 pixels).
+template <int BN, bool SWAP, bool PAIR = false>
 __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ GemmParams p) {
-  constexpr int STAGES = stages_for(BN);
-  constexpr uint32_t B_PART = (uint32_t)BN * 128u;
-  constexpr uint32_t STAGE = stage_bytes(BN);
+  constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows staged by this CTA
+  constexpr int STAGES = stages_for(BROWS);
+  constexpr uint32_t B_PART = (uint32_t)BROWS * 128u;
+  constexpr uint32_t STAGE = stage_bytes(BROWS);
   constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
   constexpr int CH = BN < 32 ? BN : 32;
-  constexpr uint32_t IDESC = idesc_bf16_f32(BN);
+  constexpr uint32_t IDESC = idesc_bf16_f32(BN, PAIR ? 256 : 128);
+  static_assert(!(PAIR && SWAP), "CTA pairs use pixel-major tiles");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -362,6 +377,9 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int rank = PAIR ? (int)cluster_ctarank() : 0;
+  const int tfirst = PAIR ? blockIdx.x / 2 : blockIdx.x;  // this CTA's (pair's) first tile
+  const int tstep = PAIR ? gridDim.x / 2 : gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -370,7 +388,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
     }
     for (int a = 0; a < 2; a++) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 256);
+      mbar_init(tempty_bar(a), PAIR ? 16 : 256);  // pairs: one release per epilogue warp of both CTAs
     }
     fence_mbar_init();
   }
@@ -379,13 +397,29 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
     for (int i = 0; i < GEMM_MAX_AMAPS; i++) tma_prefetch(&p.amap[i]);
   }
   if (warp == 2) {
-    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // epilogue release of an accumulator buffer (pairs: on the even CTA's barrier)
+  auto release = [&](int a) {
+    tc_fence_before();
+    if constexpr (PAIR) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(tempty_bar(a), 0));
+    } else {
+      mbar_arrive(tempty_bar(a));
+    }
+  };
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
@@ -395,13 +429,14 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile(p, t);
+      for (int t = tfirst; t < p.total_tiles && ok; t += tstep) {
+        const TileInfo ti = decode_tile(p, t, rank);
         const GemmClass& C = p.cls[ti.cls];
         int seg = 0;
         for (int kb = 0; kb < C.nkb; kb++) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(full_bar(stage), STAGE);
+          const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), PAIR ? 2 * STAGE : STAGE);
           const uint32_t sa = smem0 + (uint32_t)stage * STAGE;
           // activation sub-boxes: the A operand, or the B operand when swapped
           const uint32_t act = SWAP ? sa + 2 * A_PART : sa;
@@ -415,22 +450,32 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
             const int cx = S.c0 + blk * p.cb;
             const int x = ti.j0 * S.stride + S.dx[tap];
             const int y = ti.i0 * S.stride + S.dy[tap];
-            tma_load_5d(act + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, full_bar(stage));
-            tma_load_5d(act + act_part + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 1, full_bar(stage));
+            if constexpr (PAIR) {
+              tma_load_5d_pair(act + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, fb);
+              tma_load_5d_pair(act + act_part + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 1, fb);
+            } else {
+              tma_load_5d(act + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, fb);
+              tma_load_5d(act + act_part + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 1, fb);
+            }
           }
           // weights: the B operand (BN rows), or the A operand (128 rows) when swapped
           const uint32_t wdst = SWAP ? sa : sa + 2 * A_PART;
           const uint32_t wpart = SWAP ? A_PART : B_PART;
-          const int wrow = SWAP ? ti.nt * 128 : ti.nt * BN;
-          tma_load_3d(wdst, &p.bmap[ti.cls], kb * 64, wrow, 0, full_bar(stage));
-          tma_load_3d(wdst + wpart, &p.bmap[ti.cls], kb * 64, wrow, 1, full_bar(stage));
+          const int wrow = SWAP ? ti.nt * 128 : ti.nt * BN + rank * BROWS;
+          if constexpr (PAIR) {
+            tma_load_3d_pair(wdst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
+            tma_load_3d_pair(wdst + wpart, &p.bmap[ti.cls], kb * 64, wrow, 1, fb);
+          } else {
+            tma_load_3d(wdst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
+            tma_load_3d(wdst + wpart, &p.bmap[ti.cls], kb * 64, wrow, 1, fb);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       const bool sw64 = !SWAP && (p.cb == 32);  // swapped A is the 128B-swizzled weight tile
       const uint32_t a_sbo = sw64 ? 512u : 1024u;
       const uint32_t a_layout = sw64 ? 4u : 2u;
@@ -438,8 +483,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, it++) {
-        const TileInfo ti = decode_tile(p, t);
+      for (int t = tfirst; t < p.total_tiles && ok; t += tstep, it++) {
+        const TileInfo ti = decode_tile(p, t, rank);
         const GemmClass& C = p.cls[ti.cls];
         const int acc = it & 1;
         if (!mbar_wait(tempty_bar(acc), ((it >> 1) & 1) ^ 1, p.err, 2)) { ok = false; break; }
@@ -457,14 +502,24 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
             const uint64_t a_lo = smem_desc(sa + A_PART + aoff, a_sbo, a_layout);
             const uint64_t b_hi = smem_desc(sb + k * 32, 1024u, 2u);
             const uint64_t b_lo = smem_desc(sb + B_PART + k * 32, 1024u, 2u);
-            mma_bf16(d_tmem, a_lo, b_hi, IDESC, (kb | k) != 0 ? 1u : 0u);
-            mma_bf16(d_tmem, a_hi, b_lo, IDESC, 1u);
-            mma_bf16(d_tmem, a_hi, b_hi, IDESC, 1u);
+            if constexpr (PAIR) {
+              mma_bf16_pair(d_tmem, a_lo, b_hi, IDESC, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_pair(d_tmem, a_hi, b_lo, IDESC, 1u);
+              mma_bf16_pair(d_tmem, a_hi, b_hi, IDESC, 1u);
+            } else {
+              mma_bf16(d_tmem, a_lo, b_hi, IDESC, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16(d_tmem, a_hi, b_lo, IDESC, 1u);
+              mma_bf16(d_tmem, a_hi, b_hi, IDESC, 1u);
+            }
           }
-          mma_commit(empty_bar(stage));
+          if constexpr (PAIR) mma_commit_pair(empty_bar(stage), 3);
+          else mma_commit(empty_bar(stage));
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        if (ok) mma_commit(tfull_bar(acc));
+        if (ok) {
+          if constexpr (PAIR) mma_commit_pair(tfull_bar(acc), 3);
+          else mma_commit(tfull_bar(acc));
+        }
       }
     }
   } else if (warp >= 4) {
@@ -474,8 +529,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
     const int quarter = ew & 3, half = ew >> 2;
     const int m = quarter * 32 + lane;
     int it = 0;
-    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, it++) {
-      const TileInfo ti = decode_tile(p, t);
+    for (int t = tfirst; t < p.total_tiles; t += tstep, it++) {
+      const TileInfo ti = decode_tile(p, t, rank);
       const GemmClass& C = p.cls[ti.cls];
       const int acc = it & 1;
       if (!mbar_wait(tfull_bar(acc), (it >> 1) & 1, p.err, 4)) break;
@@ -483,18 +538,16 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       const uint32_t trow = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
       if constexpr (SWAP) {
         epilogue_swapped<BN>(p, C, ti, m, trow, shift_buf + ew * 32 * SHIFT_LD, half);
-        tc_fence_before();
-        mbar_arrive(tempty_bar(acc));
+        release(acc);
         continue;
       }
       const int i = ti.i0 + m / p.bw, j = ti.j0 + m % p.bw;
-      const bool valid = (i < p.mh) && (j < p.mw);
+      const bool valid = (i < p.mh) && (j < p.mw) && !ti.dummy;
       const int oy = i * C.oy_mul + C.oy_add, ox = j * C.ox_mul + C.ox_add;
       if constexpr (BN == 32) {
         if (p.out_kind == OUT_SHIFT7_NCHW) {
           if (half) {  // one 32-column chunk: the first four epilogue warps take it
-            tc_fence_before();
-            mbar_arrive(tempty_bar(acc));
+            release(acc);
             continue;
           }
           float v[32];
@@ -517,8 +570,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
                   1.0f / (1.0f + e);
             }
           }
-          tc_fence_before();
-          mbar_arrive(tempty_bar(acc));
+          release(acc);
           continue;
         }
       }
@@ -541,8 +593,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
             if (p.ostore == 1) store_split_tma(p, stage, lane, valid, ti.b, oy, ox, C.n0 + nloc, box_x, box_y, v);
             else store_f32_tma(p, stage, lane, ti.b, C.n0 + nloc, box_x, box_y, v);
           }
-          tc_fence_before();
-          mbar_arrive(tempty_bar(acc));
+          release(acc);
           continue;
         }
       }
@@ -555,8 +606,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
         const int nloc = ti.nt * BN + ch * CH;
         if (valid && nloc < C.nvalid) epilogue_chunk<CH>(p, C, ti.b, oy, ox, nloc, v);
       }
-      tc_fence_before();
-      mbar_arrive(tempty_bar(acc));
+      release(acc);
     }
     if constexpr (tma_store_bn(BN)) {
       if (p.ostore && lane == 0) bulk_wait0();
@@ -564,28 +614,70 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
   }
 
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's remote arrives and MMAs are done
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
-template <int BN, bool SWAP = false>
-int prepare_bn() {
-  const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256 + extra_smem(BN);
-  return (int)cudaFuncSetAttribute(k_conv_gemm<BN, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+template <int BN, bool SWAP = false, bool PAIR = false>
+constexpr size_t smem_for() {
+  constexpr int brows = PAIR ? BN / 2 : BN;
+  return (size_t)stages_for(brows) * stage_bytes(brows) + 1024 + 256 + extra_smem(BN);
 }
 
-template <int BN, bool SWAP = false>
+template <int BN, bool SWAP = false, bool PAIR = false>
+int prepare_bn() {
+  return (int)cudaFuncSetAttribute(k_conv_gemm<BN, SWAP, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem_for<BN, SWAP, PAIR>());
+}
+
+template <int BN, bool SWAP = false, bool PAIR = false>
 int launch_bn(const GemmParams& p, int grid, cudaStream_t stream) {
-  const size_t smem = (size_t)stages_for(BN) * stage_bytes(BN) + 1024 + 256 + extra_smem(BN);
-  k_conv_gemm<BN, SWAP><<<grid, 384, smem, stream>>>(p);
-  return (int)cudaGetLastError();
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(384);
+    cfg.dynamicSmemBytes = smem_for<BN, SWAP, PAIR>();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, k_conv_gemm<BN, SWAP, PAIR>, p);
+  } else {
+    k_conv_gemm<BN, SWAP, PAIR><<<grid, 384, smem_for<BN, SWAP, PAIR>(), stream>>>(p);
+    return (int)cudaGetLastError();
+  }
 }
 
 }  // namespace
 
 size_t conv_gemm_smem_bytes(int bn) { return (size_t)stages_for(bn) * stage_bytes(bn) + 1024 + 256 + extra_smem(bn); }
+bool conv_gemm_pair_bn(int bn) { return bn == 128; }
+
+// Clusters of the pair kernel that fit on the current device at once.
+int conv_gemm_pair_clusters() {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(384);
+  cfg.dynamicSmemBytes = smem_for<128, false, true>();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k_conv_gemm<128, false, true>, &cfg) != cudaSuccess) return 0;
+  return n;
+}
 int conv_gemm_stages(int bn) { return stages_for(bn); }
 
 // Opt every tile width into its dynamic shared memory size on the current
@@ -598,11 +690,13 @@ int conv_gemm_prepare() {
   if ((e = prepare_bn<128>())) return e;
   if ((e = prepare_bn<192>())) return e;
   if ((e = prepare_bn<256, true>())) return e;
+  if ((e = prepare_bn<128, false, true>())) return e;
   return prepare_bn<256>();
 }
 
 int launch_conv_gemm(const GemmParams& p, int bn, int grid, cudaStream_t stream) {
   if (p.swap) return bn == 256 ? launch_bn<256, true>(p, grid, stream) : -1;
+  if (p.pair) return bn == 128 ? launch_bn<128, false, true>(p, grid, stream) : -1;
   switch (bn) {
     case 16: return launch_bn<16>(p, grid, stream);
     case 32: return launch_bn<32>(p, grid, stream);

@@ -577,6 +577,7 @@ struct lama_engine {
   int* d_err = nullptr;
   int tiling = LAMA_TILING_AUTO;
   int spectral = LAMA_SPECTRAL_AUTO;
+  int pair_clusters = 0;  // co-resident CTA-pair clusters (0: no pair tiles)
   std::map<std::tuple<int, int, int, int, int, int, int>, std::unique_ptr<Plan>> plans;
 };
 
@@ -630,18 +631,16 @@ struct Builder {
     int max_stride = 1;
     for (auto& a : amaps) max_stride = std::max(max_stride, a.stride);
     // Swapped tiles (M = 128 output channels, N = 256 pixels) stage more MACs per
-    // byte; used when every class has a multiple of 128 channels and the
-    // swapped tiling still gives every SM work.
-    bool swap = allow_swap && e.tiling != LAMA_TILING_PIXEL && step_x == 0 && force_bn == 0 && cb == 64 &&
+    // byte and apply when every class has a multiple of 128 channels.  Measured:
+    // since split outputs leave through TMA stores (pixel-major tiles only),
+    // pixel-major tiles beat swapped ones for the FFC layers at batch 1 and 32
+    // and for the FourierUnit conv, so only LAMA_TILING_SWAPPED selects them.
+    bool swap = allow_swap && e.tiling == LAMA_TILING_SWAPPED && step_x == 0 && force_bn == 0 && cb == 64 &&
                 (o.kind == OUT_SPLIT || o.kind == OUT_F32_NHWC);
     for (auto& c : classes) swap = swap && c.nvalid % 128 == 0;
     int bh = 1, bw = 128;
     if (swap) {
       choose_tile(mh, mw, bh, bw, 256, max_stride);
-      long long t = 0;
-      for (auto& c : classes)
-        t += (long long)B * ((mh + bh - 1) / bh) * ((mw + bw - 1) / bw) * (c.nvalid / 128);
-      if (t < e.sms && e.tiling != LAMA_TILING_SWAPPED) swap = false;
     }
     if (!swap) {
       bh = 1;
@@ -664,6 +663,11 @@ struct Builder {
     const int bn = swap ? 256 : force_bn ? force_bn : choose_bn(ns, p.m_tiles);
     if (!bn) throw EngineError{LAMA_EUNSUPPORTED, name + ": no tile width divides the output channels"};
     op.bn = bn;
+    // CTA pairs (256 x BN tiles over two SMs) where the kernel has them and
+    // there are enough tiles for every SM
+    const bool pair = !swap && conv_gemm_pair_bn(bn) && e.pair_clusters > 0 &&
+                      (e.tiling == LAMA_TILING_PAIRED || (e.tiling == LAMA_TILING_AUTO && p.m_tiles >= 2 * e.sms));
+    p.pair = pair ? 1 : 0;
     for (size_t i = 0; i < amaps.size(); i++)
       p.amap[i] = act_map(amaps[i].act, cb, bw, bh, amaps[i].stride, amaps[i].interior);
     for (size_t i = amaps.size(); i < (size_t)GEMM_MAX_AMAPS; i++) p.amap[i] = p.amap[0];
@@ -673,7 +677,7 @@ struct Builder {
       const ClassSpec& cs = classes[ci];
       GemmClass& C = p.cls[ci];
       const WClass& wc = Wt.cls[cs.wc];
-      p.bmap[ci] = w_map(wc, swap ? 128 : bn);
+      p.bmap[ci] = w_map(wc, swap ? 128 : pair ? bn / 2 : bn);
       C.n0 = cs.n0;
       C.nvalid = cs.nvalid;
       C.ntiles_n = swap ? cs.nvalid / 128 : (cs.nvalid + bn - 1) / bn;
@@ -700,7 +704,7 @@ struct Builder {
       if (C.nkb * 64 != wc.k)
         throw EngineError{LAMA_EUNSUPPORTED, name + ": K mismatch between plan and packed weights"};
       C.tile0 = tile0;
-      tile0 += p.m_tiles * C.ntiles_n;
+      tile0 += (pair ? (p.m_tiles + 1) / 2 : p.m_tiles) * C.ntiles_n;
     }
     p.total_tiles = tile0;
     p.scale = Wt.scale;
@@ -737,7 +741,7 @@ struct Builder {
       }
       p.obox_w = std::min(bw, 32);
     }
-    op.grid = std::min(p.total_tiles, e.sms);
+    op.grid = pair ? 2 * std::min(p.total_tiles, e.pair_clusters) : std::min(p.total_tiles, e.sms);
     op.out_ptr = o.p;
     op.out_split = o.kind == OUT_SPLIT;
     op.out_part = o.part;
@@ -1082,6 +1086,7 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
     e->sms = prop.multiProcessorCount;
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     CKL(conv_gemm_prepare());
+    e->pair_clusters = conv_gemm_pair_clusters();
     CKL(fft_prepare(kFftSmem));
     CKL(fft_reg_prepare());
     e->d_err = (int*)e->wmem.alloc(256);
@@ -1181,7 +1186,7 @@ int lama_resblocks_device(lama_engine* e, const float* d_local_in, const float* 
 
 int lama_set_tiling(lama_engine* e, int policy) {
   return guarded(e, [&] {
-    if (policy < LAMA_TILING_AUTO || policy > LAMA_TILING_PIXEL) throw EngineError{LAMA_EINVAL, "unknown tiling policy"};
+    if (policy < LAMA_TILING_AUTO || policy > LAMA_TILING_PAIRED) throw EngineError{LAMA_EINVAL, "unknown tiling policy"};
     CK(cudaStreamSynchronize(e->stream));
     e->plans.clear();
     e->tiling = policy;

@@ -76,6 +76,8 @@ struct GemmParams {
   GemmClass cls[GEMM_MAX_CLASSES];
   int nclass;
   int swap;                   // 1: M = 128 output channels, N = BN pixels (see conv_gemm.cu)
+  int pair;                   // 1: clusters of two CTAs, 256 x BN tiles (see conv_gemm.cu); the grid is
+                              //    2 x clusters and tiles count pair tiles
   int cb;                     // channels per A sub-box: 64 (128B swizzle) or 32 (64B swizzle)
   int batch, mh, mw;          // M space: images x rows x cols
   int bh, bw;                 // tile rows x cols, bh * bw == 128
@@ -101,5 +103,7 @@ int launch_conv_gemm(const GemmParams& p, int bn, int grid, cudaStream_t stream)
 size_t conv_gemm_smem_bytes(int bn);
 int conv_gemm_stages(int bn);
 int conv_gemm_prepare();
+bool conv_gemm_pair_bn(int bn);  // tile widths with a CTA-pair kernel
+int conv_gemm_pair_clusters();   // co-resident clusters of the pair kernel (after conv_gemm_prepare)
 
 }  // namespace lama

@@ -174,7 +174,7 @@ class Engine:
     def stream(self) -> int:
         return lib().lama_stream(self._h) or 0
 
-    TILING_AUTO, TILING_SWAPPED, TILING_PIXEL = 0, 1, 2
+    TILING_AUTO, TILING_SWAPPED, TILING_PIXEL, TILING_PAIRED = 0, 1, 2, 3
 
     def set_tiling(self, policy: int):
         """Tile policy for plans built from now on (see include/lama_b200.h)."""

@@ -186,9 +186,10 @@ def test_full_size_512_batch_properties(engine_baseline):
     np.testing.assert_array_equal(a, engine_baseline.forward(xs))
 
 
-@pytest.mark.parametrize("policy", [1, 2])
+@pytest.mark.parametrize("policy", [1, 2, 3])
 def test_tiling_policies_compute_the_same_pass(engine_tamed, oracle_tamed, policy):
-    """Channel-major (swapped) and pixel-major GEMM tiles both match the oracle."""
+    """Channel-major (swapped), pixel-major and CTA-pair GEMM tiles all match
+    the oracle (odd tile counts give CTA pairs a dummy second tile)."""
     try:
         engine_tamed.set_tiling(policy)
         for h, w, seed in [(64, 64, 61), (72, 56, 62), (128, 96, 63)]:
@@ -251,7 +252,10 @@ def test_swapped_tiles_match_pixel_tiles_on_the_baseline_stack(engine_baseline):
         a = engine_baseline.resblocks(l, g, 18)
         engine_baseline.set_tiling(2)
         b = engine_baseline.resblocks(l, g, 18)
+        engine_baseline.set_tiling(3)
+        c = engine_baseline.resblocks(l, g, 18)
     finally:
         engine_baseline.set_tiling(0)
     scale = max(np.abs(b[0]).max(), np.abs(b[1]).max())
     assert np.abs(a[0] - b[0]).max() / scale < 1e-3 and np.abs(a[1] - b[1]).max() / scale < 1e-3
+    assert np.abs(c[0] - b[0]).max() / scale < 1e-3 and np.abs(c[1] - b[1]).max() / scale < 1e-3
