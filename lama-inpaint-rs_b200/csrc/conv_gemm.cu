@@ -94,7 +94,8 @@ __device__ __forceinline__ int reflect_idx(int i, int n) {
 __device__ __forceinline__ int halo_targets(int q, int n, int halo, int reflect, int* out) {
   int cnt = 0;
   out[cnt++] = q + halo;
-  if (reflect && halo > 0) {
+  // only interior positions within `halo` of an edge are reflected into the halo
+  if (reflect && halo > 0 && (q <= halo || q >= n - 1 - halo)) {
     for (int p = 0; p < halo; p++)
       if (reflect_idx(p - halo, n) == q) out[cnt++] = p;
     for (int p = n + halo; p < n + 2 * halo; p++)
@@ -206,8 +207,8 @@ __device__ __forceinline__ void store_split_halo(const GemmParams& p, int b, int
 // fp32 store of one warp's 32 pixels x 32 channels through the TMA unit
 // (ostore 2: NCHW, the staging tile is [channel][pixel]; ostore 3: NHWC,
 // [pixel][channel] with the 128-byte swizzle).
-__device__ __forceinline__ void store_f32_tma(const GemmParams& p, uint8_t* stage, int lane, int b, int n, int box_x,
-                                              int box_y, const float* v) {
+__device__ __forceinline__ void store_f32_tma(const GemmParams& p, const void* omap, uint8_t* stage, int lane, int b,
+                                              int n, int box_x, int box_y, const float* v) {
   if (lane == 0) bulk_wait_read0();
   __syncwarp();
   if (p.ostore == 2) {
@@ -223,8 +224,8 @@ __device__ __forceinline__ void store_f32_tma(const GemmParams& p, uint8_t* stag
   fence_async_smem();
   __syncwarp();
   if (lane == 0) {
-    if (p.ostore == 2) tma_store_4d(&p.omap, smem_u32(stage), box_x, box_y, n, b);
-    else tma_store_4d(&p.omap, smem_u32(stage), n, box_x, box_y, b);
+    if (p.ostore == 2) tma_store_4d(omap, smem_u32(stage), box_x, box_y, n, b);
+    else tma_store_4d(omap, smem_u32(stage), n, box_x, box_y, b);
     bulk_commit();
   }
 }
@@ -234,8 +235,9 @@ __device__ __forceinline__ void store_f32_tma(const GemmParams& p, uint8_t* stag
 // layout omap's box expects), one lane issues the hi and lo box stores, and
 // border lanes add their reflected halo copies with ordinary stores.  The
 // previous chunk's stores must have read the staging tile first.
-__device__ __forceinline__ void store_split_tma(const GemmParams& p, uint8_t* stage, int lane, bool valid, int b,
-                                                int oy, int ox, int n, int box_x, int box_y, const float* v) {
+__device__ __forceinline__ void store_split_tma(const GemmParams& p, const void* omap, uint8_t* stage, int lane,
+                                                bool valid, int b, int oy, int ox, int n, int box_x, int box_y,
+                                                const float* v) {
   uint32_t hi[16], lo[16];
 #pragma unroll
   for (int k = 0; k < 16; k++) split_pair(v[2 * k], v[2 * k + 1], hi[k], lo[k]);
@@ -252,8 +254,8 @@ __device__ __forceinline__ void store_split_tma(const GemmParams& p, uint8_t* st
   fence_async_smem();
   __syncwarp();
   if (lane == 0) {
-    tma_store_5d(&p.omap, smem_u32(stage), n, box_x, box_y, b, 0);
-    tma_store_5d(&p.omap, smem_u32(stage + 2048), n, box_x, box_y, b, 1);
+    tma_store_5d(omap, smem_u32(stage), n, box_x, box_y, b, 0);
+    tma_store_5d(omap, smem_u32(stage + 2048), n, box_x, box_y, b, 1);
     bulk_commit();
   }
   if (valid && p.out_halo && p.out_reflect) store_split_halo(p, b, oy, ox, n, hi, lo);
@@ -394,6 +396,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
   }
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < p.nclass; i++) tma_prefetch(&p.bmap[i]);
+    if (p.ostore)
+      for (int i = 0; i < p.nclass; i++) tma_prefetch(&p.omap[i]);
     for (int i = 0; i < GEMM_MAX_AMAPS; i++) tma_prefetch(&p.amap[i]);
   }
   if (warp == 2) {
@@ -578,8 +582,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
         if (p.ostore) {
           // box origin: the warp's first pixel (32 consecutive M rows)
           const int m0 = quarter * 32;
-          const int box_x = ti.j0 + m0 % p.bw + C.ox_add + p.out_halo;
-          const int box_y = ti.i0 + m0 / p.bw + C.oy_add + p.out_halo;
+          const int box_x = ti.j0 + m0 % p.bw, box_y = ti.i0 + m0 / p.bw;  // M-space (class grid)
+          const void* omap = &p.omap[ti.cls];
           uint8_t* stage = smem + STAGES * STAGE + STAGING_OFF + ew * STAGING_WARP;
 #pragma unroll 1
           for (int ch = half; ch < BN / 32; ch += 2) {
@@ -590,8 +594,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
             if (nloc >= C.nvalid) continue;
             affine_relu<32>(p, C, nloc, v);
             if (valid) finish_channels<32>(p, ti.b, oy, ox, C.n0 + nloc, v);
-            if (p.ostore == 1) store_split_tma(p, stage, lane, valid, ti.b, oy, ox, C.n0 + nloc, box_x, box_y, v);
-            else store_f32_tma(p, stage, lane, ti.b, C.n0 + nloc, box_x, box_y, v);
+            if (p.ostore == 1) store_split_tma(p, omap, stage, lane, valid, ti.b, oy, ox, C.n0 + nloc, box_x, box_y, v);
+            else store_f32_tma(p, omap, stage, lane, ti.b, C.n0 + nloc, box_x, box_y, v);
           }
           release(acc);
           continue;

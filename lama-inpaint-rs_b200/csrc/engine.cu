@@ -149,19 +149,23 @@ CUtensorMap act_map(const Act& a, int cb, int bw, int bh, int stride, bool inter
   return m;
 }
 
-// Split output addressed from its padded origin with extents W + halo, H + halo:
-// interior boxes start at (x + halo, y + halo) and are clipped at the far
-// edges, so they never touch the trailing halo (written by reflection).
-CUtensorMap out_map(void* p, long long part, int B, int C, int H, int W, int halo, int bw) {
+// Split output pixels (y, x) = (i * mul_y + add_y, j * mul_x + add_x) of one
+// tile class as a dense (C, j, i, B, part) grid starting at the class's first
+// interior pixel; boxes clip at the interior's far edges, so they never touch
+// the trailing halo (written by reflection).
+CUtensorMap out_map(void* p, long long part, int B, int C, int H, int W, int halo, int bw, int mul_y, int add_y,
+                    int mul_x, int add_x) {
   CUtensorMap m;
   const int hp = H + 2 * halo, wp = W + 2 * halo;
-  cuuint64_t dims[5] = {(cuuint64_t)C, (cuuint64_t)(W + halo), (cuuint64_t)(H + halo), (cuuint64_t)B, 2};
-  cuuint64_t strides[4] = {(cuuint64_t)C * 2, (cuuint64_t)wp * C * 2, (cuuint64_t)hp * wp * C * 2,
+  char* base = (char*)p + (((size_t)(add_y + halo) * wp + add_x + halo) * C) * 2;
+  cuuint64_t dims[5] = {(cuuint64_t)C, (cuuint64_t)((W - add_x + mul_x - 1) / mul_x),
+                        (cuuint64_t)((H - add_y + mul_y - 1) / mul_y), (cuuint64_t)B, 2};
+  cuuint64_t strides[4] = {(cuuint64_t)C * 2 * mul_x, (cuuint64_t)wp * C * 2 * mul_y, (cuuint64_t)hp * wp * C * 2,
                            (cuuint64_t)part * 2};
   const int bx = std::min(bw, 32);
   cuuint32_t box[5] = {32, (cuuint32_t)bx, (cuuint32_t)(32 / bx), 1, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, p, dims, strides, box, estr,
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, base, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -721,22 +725,27 @@ struct Builder {
     p.out_reflect = o.reflect;
     p.skip = o.skip;
     p.err = e.d_err;
-    // split outputs of pixel-major tiles with dense placement leave through TMA stores
-    // (TMA boxes need a 16-byte aligned innermost coordinate: channel starts on
-    // multiples of 32; for NCHW, whose innermost coordinate is x, tile
-    // columns on multiples of 4)
-    bool dense = true, x4 = bw % 4 == 0 && o.w % 4 == 0;  // NCHW rows must also be 16-byte strides
+    // outputs of pixel-major tiles leave through TMA stores (TMA boxes need a
+    // 16-byte aligned innermost coordinate: channel starts on multiples of
+    // 32; fp32 NCHW, whose innermost coordinate is x, needs dense placement
+    // and 16-byte rows and tile columns)
+    bool aligned = o.c % 32 == 0, dense = true;
     for (auto& c : classes) {
-      dense = dense && c.oy_mul == 1 && c.ox_mul == 1 && c.n0 % 32 == 0;
-      x4 = x4 && c.ox_add % 4 == 0;
+      aligned = aligned && c.n0 % 32 == 0;
+      dense = dense && c.oy_mul == 1 && c.ox_mul == 1 && c.oy_add == 0 && c.ox_add == 0;
     }
-    if (!swap && (bn == 64 || bn == 128 || bn == 192) && o.c % 32 == 0 && dense && p.step_x == bw &&
+    if (!swap && (bn == 64 || bn == 128 || bn == 192) && aligned && p.step_x == bw &&
         (bw >= 32 ? bw % 32 == 0 : 32 % bw == 0)) {
       if (o.kind == OUT_SPLIT) {
-        p.omap = out_map(o.p, o.part, B, o.c, o.h, o.w, o.halo, bw);
+        for (size_t ci = 0; ci < classes.size(); ci++) {
+          const ClassSpec& c = classes[ci];
+          p.omap[ci] = out_map(o.p, o.part, B, o.c, o.h, o.w, o.halo, bw, c.oy_mul, c.oy_add, c.ox_mul, c.ox_add);
+        }
         p.ostore = 1;
-      } else if ((o.kind == OUT_F32_NHWC || (o.kind == OUT_F32_NCHW && x4)) && o.halo == 0) {
-        p.omap = out_map_f32(o.p, o.kind == OUT_F32_NCHW, B, o.c, o.h, o.w, bw);
+      } else if (dense && o.halo == 0 &&
+                 (o.kind == OUT_F32_NHWC || (o.kind == OUT_F32_NCHW && bw % 4 == 0 && o.w % 4 == 0))) {
+        for (size_t ci = 0; ci < classes.size(); ci++)
+          p.omap[ci] = out_map_f32(o.p, o.kind == OUT_F32_NCHW, B, o.c, o.h, o.w, bw);
         p.ostore = o.kind == OUT_F32_NCHW ? 2 : 3;
       }
       p.obox_w = std::min(bw, 32);

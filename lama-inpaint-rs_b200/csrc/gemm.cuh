@@ -67,11 +67,13 @@ struct GemmParams {
   CUtensorMap bmap[GEMM_MAX_CLASSES];
   // ostore != 0: the output leaves through TMA tensor stores of one box per
   // epilogue warp and 32-channel chunk (32 channels x obox_w x 32 / obox_w
-  // pixels).  1 = split: omap is (C, W + h, H + h, B, part) from the padded
-  // origin (boxes clip at the interior's far edges, the trailing halo is
-  // written by reflection), 64-byte swizzled; 2 = fp32 NCHW: (W, H, C, B);
-  // 3 = fp32 NHWC: (C, W, H, B), 128-byte swizzled.
-  CUtensorMap omap;
+  // pixels).  omap[c] views class c's output pixels (output = M pixel * mul +
+  // add) as a dense grid indexed by M-space (j, i): 1 = split,
+  // (C, W/mul, H/mul, B, part) from the class's first interior pixel, 64-byte
+  // swizzled (boxes clip at the interior's far edges; reflected halo copies
+  // are ordinary stores); 2 = fp32 NCHW (W, H, C, B); 3 = fp32 NHWC
+  // (C, W, H, B), 128-byte swizzled.
+  CUtensorMap omap[GEMM_MAX_CLASSES];
   int ostore, obox_w;
   GemmClass cls[GEMM_MAX_CLASSES];
   int nclass;
@@ -97,6 +99,8 @@ struct GemmParams {
   const void* skip;           // split residual, same geometry as out (may alias it)
   int* err;                   // device status word (0 = ok)
 };
+
+static_assert(sizeof(GemmParams) <= 4096, "GemmParams must fit the kernel parameter space");
 
 // Host launcher (conv_gemm.cu).  `bn` in {16, 32, 64, 128, 192, 256}.
 int launch_conv_gemm(const GemmParams& p, int bn, int grid, cudaStream_t stream);
