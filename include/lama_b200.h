@@ -173,9 +173,15 @@ int lama_section_rects(const uint8_t* mask, int w, int h, int* out, int cap);
 
 /* No counterpart in the reference: the FourierUnit's forward transform
  * (rfft2, norm='ortho', the reference's transform directions) on its own,
- * for callers that cannot allocate device memory.  It runs the two-pass
- * kernels with their intermediate in a fixed device array compiled into the
- * library and calls no cudaMalloc / cudaFree.
+ * for callers that cannot allocate device memory (a host whose HBM is
+ * already reserved by another framework's pool, or a pipeline that cannot
+ * take the device-wide synchronisation of cudaMalloc / cudaFree between its
+ * launches).  It runs the two-pass kernels with their intermediate in a fixed
+ * 16 MiB device array compiled into the library (held by every GPU that
+ * loads the library, until exit) and calls no cudaMalloc / cudaFree.  The
+ * first call on a device does that device's one-time set-up (it looks up the
+ * array's device address and sets the kernels' shared-memory limit), so make
+ * it before any stream capture on that device.
  *   d_feat: [batch][channels][h][w] fp32 (device);
  *   d_spec: [2][batch][h][w/2+1][2*channels] bf16 (device), value = part 0 +
  *           part 1, channel 2c = real and 2c+1 = imaginary part of channel c
@@ -184,8 +190,10 @@ int lama_section_rects(const uint8_t* mask, int w, int h, int* out, int cap);
  * complex fp32); larger requests return LAMA_ESCRATCH.  Work is queued on
  * `stream` (a cudaStream_t, null = legacy default stream) of CUDA device
  * `device`; the caller's current device is restored.  Every call shares the
- * one array: calls whose GPU work overlaps in time race.  On failure a
- * message is written to err (err_len bytes, may be null). */
+ * one array and leaves its contents behind; nothing in it needs to start at
+ * zero (each call overwrites what it reads), but calls whose GPU work
+ * overlaps in time race.  On failure a message is written to err (err_len
+ * bytes, may be null). */
 int lama_rfft2_noalloc(int device, const float* d_feat, int batch, int channels, int h, int w, void* d_spec,
                        void* stream, char* err, int err_len);
 

@@ -8,7 +8,11 @@
 // pass before the column pass reads it, the tables are copied in by each
 // call), and calls whose GPU work overlaps in time - on different streams,
 // or from several host threads - race on it.  The entry point calls no
-// cudaMalloc, cudaFree or other allocating routine.
+// cudaMalloc, cudaFree or other allocating routine.  Host code cannot use the
+// array's name as a device pointer: the first call on each device, with that
+// device current, looks up its address (cudaGetSymbolAddress) and sets the
+// kernels' shared-memory limit; that first call belongs before any stream
+// capture on the device.
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
