@@ -219,17 +219,23 @@ def test_spectral_paths_compute_the_same_pass(engine_tamed, oracle_tamed, path):
         engine_tamed.set_spectral_path(0)
 
 
-@pytest.mark.parametrize("h,w", [(1024, 1024), (2048, 2048), (600, 600), (520, 776)])
-def test_two_pass_spectral_kernels_on_large_latents(engine_tamed, h, w):
+@pytest.mark.parametrize("h,w,path", [(512, 512, 1), (512, 512, 2), (256, 128, 2), (1024, 1024, 0),
+                                      (2048, 2048, 0), (600, 600, 0), (520, 776, 0)])
+def test_spectral_kernels_on_large_latents(engine_tamed, h, w, path):
     """rfft2 and irfft2 (+ the FourierUnit residual) of the first resblock at
-    latents 128^2, 256^2, 75^2 (the --tile window of
-    config 2) and 65x97 against float64 torch with the reference's transform
-    directions, on the engine's own conv1 / FourierUnit-conv outputs."""
+    latents 64^2 (both spectral paths), 32x16 (register path), 128^2, 256^2
+    75^2 (the --tile window of config 2) and 65x97
+    against float64 torch with the reference's transform directions, on the
+    engine's own conv1 / FourierUnit-conv outputs."""
     from torch_ref import irfft2_ortho, rfft2_ortho
     _, _, x = make_input(h, w, 81)
     lh, lw = h // 8, w // 8
-    engine_tamed.debug_run(x, 9)
-    reads = {op: engine_tamed.debug_read(1, h, w, op) for op in (5, 6, 7, 8)}
+    try:
+        engine_tamed.set_spectral_path(path)
+        engine_tamed.debug_run(x, 9)
+        reads = {op: engine_tamed.debug_read(1, h, w, op) for op in (5, 6, 7, 8)}
+    finally:
+        engine_tamed.set_spectral_path(0)
     assert [reads[op][0] for op in (5, 6, 7, 8)] == ["spectral_conv1", "rfft2", "fourier_conv", "irfft2"]
     feat = torch.from_numpy(reads[5][1].reshape(1, 192, lh, lw)).double()
     sp = rfft2_ortho(feat)
