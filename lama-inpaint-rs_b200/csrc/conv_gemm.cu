@@ -57,7 +57,10 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
 
 struct TileInfo {
   int cls, nt, b, i0, j0;
-  bool dummy;  // CTA-pair tile past the class's last M tile (loads zeros, stores nothing)
+  bool dummy;      // CTA-pair tile past the class's last M tile (loads zeros, stores nothing)
+  int kb0, kb1;    // K blocks of this tile (a part of the class's K with split-K)
+  int part;        // split-K part of this tile
+  int split_tile;  // split-K: workspace slice of part 0 of this output tile (slices part 0..ksplit-1 follow)
 };
 
 // Tile t of the launch.  With CTA pairs (p.pair) t counts pair tiles: the
@@ -69,8 +72,14 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t, int 
   const GemmClass& C = p.cls[c];
   int lt = t - C.tile0;
   ti.cls = c;
+  const int part = lt % C.ksplit;  // split-K parts of one output tile are consecutive tiles
+  lt /= C.ksplit;
+  ti.kb0 = part * C.nkb / C.ksplit;
+  ti.kb1 = (part + 1) * C.nkb / C.ksplit;
+  ti.part = part;
   ti.nt = lt % C.ntiles_n;
   int mt = lt / C.ntiles_n;
+  ti.split_tile = C.ws_tile0 + (mt * C.ntiles_n + ti.nt) * C.ksplit;
   if (p.pair) mt = 2 * mt + rank;
   ti.dummy = mt >= p.m_tiles;
   int per_img = p.tiles_y * p.tiles_x;
@@ -370,6 +379,10 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  // split-K verdict of the current tile (2 * tile sequence + last) and the
+  // count of epilogue warps that have added their partial sums
+  volatile int* split_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* split_cnt = reinterpret_cast<int*>(tmem_slot + 2);
   float* shift_buf = reinterpret_cast<float*>(smem + STAGES * STAGE + 256);
   const uint32_t smem0 = smem_u32(smem);
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
@@ -388,6 +401,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
+    *split_flag = -2;
+    *split_cnt = 0;
     for (int a = 0; a < 2; a++) {
       mbar_init(tfull_bar(a), 1);
       mbar_init(tempty_bar(a), PAIR ? 16 : 256);  // pairs: one release per epilogue warp of both CTAs
@@ -437,7 +452,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
         const TileInfo ti = decode_tile(p, t, rank);
         const GemmClass& C = p.cls[ti.cls];
         int seg = 0;
-        for (int kb = 0; kb < C.nkb; kb++) {
+        for (int kb = ti.kb0; kb < ti.kb1; kb++) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, 1)) { ok = false; break; }
           const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
           if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), PAIR ? 2 * STAGE : STAGE);
@@ -489,12 +504,11 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       bool ok = true;
       for (int t = tfirst; t < p.total_tiles && ok; t += tstep, it++) {
         const TileInfo ti = decode_tile(p, t, rank);
-        const GemmClass& C = p.cls[ti.cls];
         const int acc = it & 1;
         if (!mbar_wait(tempty_bar(acc), ((it >> 1) & 1) ^ 1, p.err, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < C.nkb; kb++) {
+        for (int kb = ti.kb0; kb < ti.kb1; kb++) {
           if (!mbar_wait(full_bar(stage), phase, p.err, 3)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem0 + (uint32_t)stage * STAGE;
@@ -507,11 +521,11 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
             const uint64_t b_hi = smem_desc(sb + k * 32, 1024u, 2u);
             const uint64_t b_lo = smem_desc(sb + B_PART + k * 32, 1024u, 2u);
             if constexpr (PAIR) {
-              mma_bf16_pair(d_tmem, a_lo, b_hi, IDESC, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_pair(d_tmem, a_lo, b_hi, IDESC, (kb != ti.kb0 || k != 0) ? 1u : 0u);
               mma_bf16_pair(d_tmem, a_hi, b_lo, IDESC, 1u);
               mma_bf16_pair(d_tmem, a_hi, b_hi, IDESC, 1u);
             } else {
-              mma_bf16(d_tmem, a_lo, b_hi, IDESC, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16(d_tmem, a_lo, b_hi, IDESC, (kb != ti.kb0 || k != 0) ? 1u : 0u);
               mma_bf16(d_tmem, a_hi, b_lo, IDESC, 1u);
               mma_bf16(d_tmem, a_hi, b_hi, IDESC, 1u);
             }
@@ -578,6 +592,70 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           continue;
         }
       }
+      // split-K: every part stores its raw sums in its own workspace slice; the
+      // CTA whose part arrives last finishes the tile from the sum of the
+      // slices in part order (deterministic), the others are done
+      const bool split = (CH == 32 && !SWAP && !PAIR) && C.ksplit > 1;
+      const float* wsp = nullptr;
+      if constexpr (CH == 32 && !SWAP && !PAIR) {
+        if (split) {
+          wsp = p.ws + (size_t)ti.split_tile * (BN * 128) + m;  // slice [n][m] of part 0
+          float* mine = p.ws + (size_t)(ti.split_tile + ti.part) * (BN * 128) + m;
+#pragma unroll 1
+          for (int ch = half; ch < BN / 32; ch += 2) {
+            float v[32];
+            tmem_ld32(trow + ch * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 32; k++) __stcg(mine + (ch * 32 + k) * 128, v[k]);
+          }
+          release(acc);
+          __threadfence();
+          __syncwarp();
+          // the eighth epilogue warp to get here counts this CTA's part in and
+          // publishes (tile sequence, last?) for the others, which wait for it
+          // with a bounded spin
+          int last = 0;
+          if (lane == 0) {
+            if (atomicAdd(split_cnt, 1) == 7) {
+              *split_cnt = 0;
+              last = atomicAdd(p.cnt + ti.split_tile, 1) == C.ksplit - 1;
+              if (last) p.cnt[ti.split_tile] = 0;
+              __threadfence_block();
+              *split_flag = 2 * it + last;
+            } else {
+              const long long t0 = clock64();
+              int f;
+              while (((f = *split_flag) >> 1) != it) {
+                if (clock64() - t0 > LAMA_WAIT_CYCLES) {
+                  atomicCAS(p.err, 0, 5);
+                  f = 2 * it;
+                  break;
+                }
+              }
+              last = f & 1;
+            }
+          }
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (!last) continue;
+          __threadfence();
+        }
+      }
+      // the 32 values of chunk ch: from TMEM, or (split-K fix-up) from the workspace
+      auto chunk32 = [&](int ch, float* v) {
+        if (split) {
+#pragma unroll
+          for (int k = 0; k < 32; k++) v[k] = __ldcg(wsp + (ch * 32 + k) * 128);
+          for (int q = 1; q < C.ksplit; q++) {
+            const float* sl = wsp + (size_t)q * (BN * 128);
+#pragma unroll
+            for (int k = 0; k < 32; k++) v[k] += __ldcg(sl + (ch * 32 + k) * 128);
+          }
+        } else {
+          tmem_ld32(trow + ch * 32, v);
+          tmem_wait_ld();
+        }
+      };
       if constexpr (tma_store_bn(BN)) {
         if (p.ostore) {
           // box origin: the warp's first pixel (32 consecutive M rows)
@@ -588,8 +666,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
 #pragma unroll 1
           for (int ch = half; ch < BN / 32; ch += 2) {
             float v[32];
-            tmem_ld32(trow + ch * 32, v);
-            tmem_wait_ld();
+            chunk32(ch, v);
             const int nloc = ti.nt * BN + ch * 32;
             if (nloc >= C.nvalid) continue;
             affine_relu<32>(p, C, nloc, v);
@@ -597,20 +674,23 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
             if (p.ostore == 1) store_split_tma(p, omap, stage, lane, valid, ti.b, oy, ox, C.n0 + nloc, box_x, box_y, v);
             else store_f32_tma(p, omap, stage, lane, ti.b, C.n0 + nloc, box_x, box_y, v);
           }
-          release(acc);
+          if (!split) release(acc);
           continue;
         }
       }
 #pragma unroll 1
       for (int ch = half; ch < BN / CH; ch += 2) {
         float v[CH];
-        if constexpr (CH == 32) tmem_ld32(trow + ch * CH, v);
-        else tmem_ld16(trow + ch * CH, v);
-        tmem_wait_ld();
+        if constexpr (CH == 32) {
+          chunk32(ch, v);
+        } else {
+          tmem_ld16(trow + ch * CH, v);
+          tmem_wait_ld();
+        }
         const int nloc = ti.nt * BN + ch * CH;
         if (valid && nloc < C.nvalid) epilogue_chunk<CH>(p, C, ti.b, oy, ox, nloc, v);
       }
-      release(acc);
+      if (!split) release(acc);
     }
     if constexpr (tma_store_bn(BN)) {
       if (p.ostore && lane == 0) bulk_wait0();

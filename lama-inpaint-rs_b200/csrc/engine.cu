@@ -707,8 +707,28 @@ struct Builder {
       C.nkb = sub * cb / 64;
       if (C.nkb * 64 != wc.k)
         throw EngineError{LAMA_EUNSUPPORTED, name + ": K mismatch between plan and packed weights"};
+    }
+    // Split-K for launches too small to fill the GPU (batch-1 passes): K parts
+    // of at most ~the per-SM share of all K blocks, finished in-kernel by the
+    // last part (pixel-major single-CTA tiles, 32-column chunks, not the
+    // shifted-sum OutConv).
+    long long kbs = 0;
+    for (size_t ci = 0; ci < classes.size(); ci++) kbs += (long long)p.m_tiles * p.cls[ci].ntiles_n * p.cls[ci].nkb;
+    const int share = (int)std::max<long long>(12, (kbs + e.sms - 1) / e.sms);
+    const bool can_split = !swap && !pair && bn >= 32 && o.kind != OUT_SHIFT7_NCHW && p.step_x == bw;
+    int ws_tiles = 0;
+    for (size_t ci = 0; ci < classes.size(); ci++) {
+      GemmClass& C = p.cls[ci];
+      C.ksplit = can_split ? std::min(8, std::max(1, (C.nkb + share - 1) / share)) : 1;
+      C.ksplit = std::min(C.ksplit, C.nkb);
+      C.ws_tile0 = ws_tiles;
+      if (C.ksplit > 1) ws_tiles += p.m_tiles * C.ntiles_n * C.ksplit;  // one slice per part
       C.tile0 = tile0;
-      tile0 += (pair ? (p.m_tiles + 1) / 2 : p.m_tiles) * C.ntiles_n;
+      tile0 += (pair ? (p.m_tiles + 1) / 2 : p.m_tiles) * C.ntiles_n * C.ksplit;
+    }
+    if (ws_tiles) {
+      p.ws = (float*)pl.mem.alloc((size_t)ws_tiles * bn * 128 * sizeof(float), false);
+      p.cnt = (int*)pl.mem.alloc((size_t)ws_tiles * sizeof(int));  // zeroed; reset by each tile's finisher
     }
     p.total_tiles = tile0;
     p.scale = Wt.scale;

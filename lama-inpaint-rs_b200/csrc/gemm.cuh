@@ -59,6 +59,8 @@ struct GemmClass {
   int nseg;
   int oy_mul, oy_add, ox_mul, ox_add;  // output pixel = M pixel * mul + add
   int tile0;     // first global tile index of the class
+  int ksplit;    // K parts per output tile (split-K; 1 = none)
+  int ws_tile0;  // first workspace slice of the class (split-K)
   GemmSeg seg[GEMM_MAX_SEGS];
 };
 
@@ -97,6 +99,12 @@ struct GemmParams {
   int out_c, out_h, out_w;    // output tensor channels and interior extent
   int out_halo, out_reflect;  // halo width; fill it by reflection
   const void* skip;           // split residual, same geometry as out (may alias it)
+  // split-K (classes with ksplit > 1): fp32 partial sums, one [BN][128] slice
+  // per part of each output tile, and one arrival counter per output tile
+  // (indexed by its part-0 slice), zero between launches (the CTA that
+  // finishes a tile resets it)
+  float* ws;
+  int* cnt;
   int* err;                   // device status word (0 = ok)
 };
 
