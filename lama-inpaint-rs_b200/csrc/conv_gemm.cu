@@ -22,6 +22,7 @@
 //               ReLU, residual, sigmoid, split-bf16 or fp32 store, reflect halo
 // TMEM holds two BN-column accumulators so the epilogue of one tile overlaps
 // the main loop of the next.
+#include <algorithm>
 #include <cstdio>
 
 #include "gemm.cuh"
@@ -743,14 +744,15 @@ int launch_bn(const GemmParams& p, int grid, cudaStream_t stream) {
 }  // namespace
 
 size_t conv_gemm_smem_bytes(int bn) { return (size_t)stages_for(bn) * stage_bytes(bn) + 1024 + 256 + extra_smem(bn); }
-bool conv_gemm_pair_bn(int bn) { return bn == 128; }
+bool conv_gemm_pair_bn(int bn) { return bn == 128 || bn == 192; }
 
-// Clusters of the pair kernel that fit on the current device at once.
-int conv_gemm_pair_clusters() {
+namespace {
+template <int BN>
+int pair_clusters_for() {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2);
   cfg.blockDim = dim3(384);
-  cfg.dynamicSmemBytes = smem_for<128, false, true>();
+  cfg.dynamicSmemBytes = smem_for<BN, false, true>();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -759,13 +761,15 @@ int conv_gemm_pair_clusters() {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, k_conv_gemm<128, false, true>, &cfg) != cudaSuccess) return 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k_conv_gemm<BN, false, true>, &cfg) != cudaSuccess) return 0;
   return n;
 }
-int conv_gemm_stages(int bn) { return stages_for(bn); }
+}  // namespace
 
-// Opt every tile width into its dynamic shared memory size on the current
-// device; call once per device before the first launch.
+// Clusters of the pair kernels that fit on the current device at once (the
+// smaller of the tile widths' counts).
+int conv_gemm_pair_clusters() { return std::min(pair_clusters_for<128>(), pair_clusters_for<192>()); }
+
 int conv_gemm_prepare() {
   int e = 0;
   if ((e = prepare_bn<16>())) return e;
@@ -775,12 +779,14 @@ int conv_gemm_prepare() {
   if ((e = prepare_bn<192>())) return e;
   if ((e = prepare_bn<256, true>())) return e;
   if ((e = prepare_bn<128, false, true>())) return e;
+  if ((e = prepare_bn<192, false, true>())) return e;
   return prepare_bn<256>();
 }
 
 int launch_conv_gemm(const GemmParams& p, int bn, int grid, cudaStream_t stream) {
   if (p.swap) return bn == 256 ? launch_bn<256, true>(p, grid, stream) : -1;
-  if (p.pair) return bn == 128 ? launch_bn<128, false, true>(p, grid, stream) : -1;
+  if (p.pair) return bn == 128 ? launch_bn<128, false, true>(p, grid, stream)
+                    : bn == 192 ? launch_bn<192, false, true>(p, grid, stream) : -1;
   switch (bn) {
     case 16: return launch_bn<16>(p, grid, stream);
     case 32: return launch_bn<32>(p, grid, stream);
