@@ -151,6 +151,15 @@ int lama_debug_run(lama_engine* e, const float* in, int batch, int h, int w, int
 int lama_debug_read(lama_engine* e, int batch, int h, int w, int op, float* out, long long cap, int* dims,
                     char* name);
 
+/* Diagnostic of the failure path (SURVEY failure detection; the reference
+ * has no counterpart): launches one CTA that waits on an mbarrier nothing
+ * ever arrives on, with a limit of `limit_ms` milliseconds of SM clock
+ * instead of the pass kernels' ~1 s.  The wait gives up, records its code in
+ * the engine's device status word and returns, so the call reports
+ * LAMA_EDEVICE ("a kernel wait timed out ...") and the engine stays usable;
+ * no GPU fault or hang is involved.  limit_ms in 1..1000. */
+int lama_debug_wait_timeout(lama_engine* e, int limit_ms);
+
 /* Host helpers of the CLI's --tile / --sections modes (no GPU needed).
  * They restate lama-rs/src/main.rs's geometry with the same constants
  * (window >= 512, sections of 256, multiples of 8) and ordering. */

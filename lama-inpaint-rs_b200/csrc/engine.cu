@@ -34,6 +34,7 @@
 #include "gemm.cuh"
 #include "lama_b200.h"
 #include "pointwise.cuh"
+#include "ptx.cuh"
 #include "weights.h"
 
 using namespace lama;
@@ -1289,6 +1290,36 @@ int lama_profile_forward(lama_engine* e, const float* d_in, int batch, int h, in
       n++;
     }
     if (n_stats) *n_stats = n;
+  });
+}
+
+namespace {
+// One CTA waits on an mbarrier that never completes, with a bounded spin:
+// the same give-up path as the pass kernels' waits, with a short limit.
+__global__ void k_wait_probe(int* err, long long limit_cycles) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  const uint32_t b = smem_u32(&bar);
+  mbar_init(b, 1);
+  fence_mbar_init();
+  const long long t0 = clock64();
+  while (!mbar_try_wait(b, 0)) {
+    if (clock64() - t0 > limit_cycles) {
+      atomicCAS(err, 0, 6);
+      return;
+    }
+  }
+}
+}  // namespace
+
+int lama_debug_wait_timeout(lama_engine* e, int limit_ms) {
+  return guarded(e, [&] {
+    if (limit_ms < 1 || limit_ms > 1000) throw EngineError{LAMA_EINVAL, "limit_ms must be in 1..1000"};
+    int khz = 0;
+    CK(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, e->device));
+    k_wait_probe<<<1, 32, 0, e->stream>>>(e->d_err, (long long)khz * limit_ms);
+    CKL((int)cudaGetLastError());
+    sync_check(e);
   });
 }
 

@@ -59,6 +59,7 @@ SIGNATURES = [
                                              ctypes.c_int, _vp, _vp]),
     ("lama_set_tiling", ctypes.c_int, [_vp, ctypes.c_int]),
     ("lama_set_spectral_path", ctypes.c_int, [_vp, ctypes.c_int]),
+    ("lama_debug_wait_timeout", ctypes.c_int, [_vp, ctypes.c_int]),
     ("lama_rfft2_noalloc", ctypes.c_int, [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           _vp, _vp, ctypes.c_char_p, ctypes.c_int]),
     ("lama_last_error", ctypes.c_char_p, [_vp]),
@@ -260,6 +261,10 @@ class Engine:
             x = x[None]
         b, _, h, w = x.shape
         self._check(lib().lama_debug_run(self._h, _fp(x), b, h, w, n_ops))
+
+    def debug_wait_timeout(self, limit_ms: int):
+        """Run the bounded-wait probe (include/lama_b200.h); raises LamaError(EDEVICE)."""
+        self._check(lib().lama_debug_wait_timeout(self._h, limit_ms))
 
     def op_names(self, batch: int, h: int, w: int):
         """Launch names of the f32 forward plan at this shape, in order."""

@@ -265,3 +265,15 @@ def test_swapped_tiles_match_pixel_tiles_on_the_baseline_stack(engine_baseline):
     scale = max(np.abs(b[0]).max(), np.abs(b[1]).max())
     assert np.abs(a[0] - b[0]).max() / scale < 1e-3 and np.abs(a[1] - b[1]).max() / scale < 1e-3
     assert np.abs(c[0] - b[0]).max() / scale < 1e-3 and np.abs(c[1] - b[1]).max() / scale < 1e-3
+
+
+def test_a_device_wait_that_runs_out_is_reported_and_the_engine_recovers(engine_tamed, oracle_tamed):
+    """Failure detection without a GPU fault: a kernel wait on a barrier that
+    nothing arrives on gives up after its limit and records its code; the call
+    reports EDEVICE and the next pass on the same engine is still correct."""
+    from lama_b200.engine import LamaError
+    with pytest.raises(LamaError) as ei:
+        engine_tamed.debug_wait_timeout(20)
+    assert ei.value.code == -4 and "timed out" in ei.value.msg and "code 6" in ei.value.msg
+    _, _, x = make_input(64, 64, 91)
+    assert np.abs(engine_tamed.forward(x) - oracle_tamed.forward(x)).max() <= FLOAT_TOL
