@@ -103,13 +103,14 @@ enum { LAMA_TILING_AUTO = 0, LAMA_TILING_SWAPPED = 1, LAMA_TILING_PIXEL = 2, LAM
 int lama_set_tiling(lama_engine* e, int policy);
 
 /* Spectral-transform kernels for plans built after this call (cached plans
- * are dropped): LAMA_SPECTRAL_AUTO picks by plane size (today the same as
- * LAMA_SPECTRAL_REGISTER), LAMA_SPECTRAL_TWO_PASS always runs the two-pass
- * kernels (any plane size), LAMA_SPECTRAL_REGISTER runs the register-resident
- * kernels wherever the plane is a power of two with sides 8..64 (two-pass
- * elsewhere).  All paths
- * compute the same function; tests use this to cover each. */
-enum { LAMA_SPECTRAL_AUTO = 0, LAMA_SPECTRAL_TWO_PASS = 1, LAMA_SPECTRAL_REGISTER = 2 };
+ * are dropped): LAMA_SPECTRAL_TWO_PASS always runs the two-pass kernels (any
+ * plane size); LAMA_SPECTRAL_REGISTER runs the register-resident kernels
+ * wherever the plane is a power of two with sides 8..64 (two-pass
+ * elsewhere); LAMA_SPECTRAL_PREFETCH is REGISTER with the persistent
+ * TMA-prefetching rfft2 for 64x64 planes; LAMA_SPECTRAL_AUTO picks by plane
+ * size (today the same as PREFETCH).  All paths compute the same function;
+ * tests use this to cover each. */
+enum { LAMA_SPECTRAL_AUTO = 0, LAMA_SPECTRAL_TWO_PASS = 1, LAMA_SPECTRAL_REGISTER = 2, LAMA_SPECTRAL_PREFETCH = 3 };
 int lama_set_spectral_path(lama_engine* e, int path);
 
 /* Message of the last failure on this engine ("" if none). */

@@ -473,13 +473,14 @@ void load_weights(const WeightFile& wf, Weights& W) {
 }
 
 // ------------------------------------------------------------------ ops
-enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
+enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
 
 struct Op {
   OpKind kind;
   std::string name;
   int bn = 0, grid = 0;
   std::unique_ptr<GemmParams> g;
+  std::unique_ptr<FftPfParams> fpf;
   FftParams f{};
   UnfoldParams u{};
   CompositeParams c{};
@@ -501,6 +502,7 @@ int launch_op(const Op& op, cudaStream_t st) {
     case OP_IRFFT: return launch_irfft2(op.f, st);
     case OP_RFFT_REG: return launch_fft_reg(op.f, false, st);
     case OP_IRFFT_REG: return launch_fft_reg(op.f, true, st);
+    case OP_RFFT_PF: return launch_rfft2_pf(*op.fpf, op.grid, st);
     case OP_UNFOLD_F32: return launch_unfold_f32(op.u, st);
     case OP_UNFOLD_U8: return launch_unfold_u8(op.u, st);
     case OP_COMPOSITE: return launch_composite(op.c, st);
@@ -836,8 +838,25 @@ struct Builder {
     if (!fft_tiles(fp, kFftSmem))
       throw EngineError{LAMA_EUNSUPPORTED, "latent plane " + std::to_string(h) + "x" + std::to_string(w) +
                                                " needs more shared memory than the spectral kernels have"};
+    fp.err = e.d_err;
     const bool reg = fft_reg_supported(h, w) && use_reg_fft();
     if (!reg) fp.tmp = (float2*)pl.mem.alloc(fft_tmp_elems(fp) * sizeof(float2));
+    // the prefetching rfft2 beats the register one at batch 1, 8 and 32 (64x64 planes)
+    const bool pf = (e.spectral == LAMA_SPECTRAL_PREFETCH || e.spectral == LAMA_SPECTRAL_AUTO) &&
+                    fft_pf_supported(192, h, w);
+    CUtensorMap feat_map{};
+    if (pf) {
+      // feat as rows of 64 floats, boxes of 32 floats x 256 rows (4 channels' x-halves)
+      cuuint64_t dims[2] = {64, (cuuint64_t)B * 192 * 64};
+      cuuint64_t strides[1] = {256};
+      cuuint32_t box[2] = {32, 256};
+      cuuint32_t estr[2] = {1, 1};
+      CUresult r = encode_fn()(&feat_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, feat, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS)
+        throw EngineError{LAMA_ECUDA, "cuTensorMapEncodeTiled (feat rows) failed: " + std::to_string((int)r)};
+    }
     const double px = (double)B * h * w, pxs = (double)B * h * wh;
     for (int blk = 0; blk < nblocks; blk++)
       for (int sub = 0; sub < 2; sub++) {
@@ -849,9 +868,13 @@ struct Builder {
         gemm("spectral_conv1", F.conv1, {{Xin, 1, false}}, {one_seg(0, 0, 192, SegSpec{0, 128, 384, 1, {{1, 1}}})}, 64, B, h, w,
              OutSpec{OUT_F32_NCHW, feat, 0, 192, h, w, 0, 0, nullptr}, 1, 0, 2.0 * px * 192 * 384);
         Op r;
-        r.kind = reg ? OP_RFFT_REG : OP_RFFT;
+        r.kind = pf ? OP_RFFT_PF : reg ? OP_RFFT_REG : OP_RFFT;
         r.name = "rfft2";
         r.f = fp;
+        if (pf) {
+          r.fpf.reset(new FftPfParams{feat_map, fp});
+          r.grid = std::min(B * 192 / 4, e.sms);
+        }
         r.bytes = px * 192 * 4 + pxs * 384 * 4;
         r.out_ptr = spec.p; r.out_split = 1; r.out_part = spec.part();
         r.dims[0] = B; r.dims[1] = h; r.dims[2] = wh; r.dims[3] = 384;
@@ -1119,6 +1142,7 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
     e->pair_clusters = conv_gemm_pair_clusters();
     CKL(fft_prepare(kFftSmem));
     CKL(fft_reg_prepare());
+    CKL(fft_pf_prepare());
     e->d_err = (int*)e->wmem.alloc(256);
     upload_weights(e->W, e->wmem);
   } catch (const EngineError& x) {
@@ -1225,7 +1249,7 @@ int lama_set_tiling(lama_engine* e, int policy) {
 
 int lama_set_spectral_path(lama_engine* e, int path) {
   return guarded(e, [&] {
-    if (path < LAMA_SPECTRAL_AUTO || path > LAMA_SPECTRAL_REGISTER) throw EngineError{LAMA_EINVAL, "unknown spectral path"};
+    if (path < LAMA_SPECTRAL_AUTO || path > LAMA_SPECTRAL_PREFETCH) throw EngineError{LAMA_EINVAL, "unknown spectral path"};
     CK(cudaStreamSynchronize(e->stream));
     e->plans.clear();
     e->spectral = path;

@@ -1,6 +1,7 @@
 // FourierUnit transform kernels (fft.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -59,6 +60,14 @@ struct FftParams {
   float2* tmp;             // fft.cu: intermediate, fft_tmp_elems(p) complex values
   Radices rad_h, rad_w;    // fft.cu: stages of the column / row transforms
   FastDiv fd_w, fd_h, fd_cg, fd_kb, fd_rows;  // fft.cu: w, h, cg, kb, 2 * rp
+  int* err;                // device status word (bounded waits of the prefetching kernel)
+};
+
+// The prefetching rfft2 of 64 x 64 planes (fft_reg.cu): feat_map views feat
+// as rows (x: 64 floats, rows: B * c * 64), boxes of 32 x 256, 128-byte swizzle.
+struct FftPfParams {
+  CUtensorMap feat_map;
+  FftParams p;
 };
 
 // Two-pass kernels for any plane size (fft.cu).  fft_tiles fills cg/kb/rp/rpi
@@ -75,6 +84,9 @@ int launch_irfft2(const FftParams& p, cudaStream_t st);
 // Register-resident kernels for power-of-two planes with sides in {8..64}
 // (fft_reg.cu).
 bool fft_reg_supported(int h, int w);
+bool fft_pf_supported(int c, int h, int w);
+int fft_pf_prepare();
+int launch_rfft2_pf(const FftPfParams& q, int grid, cudaStream_t st);
 int fft_reg_prepare();
 int launch_fft_reg(const FftParams& p, bool inverse, cudaStream_t st);
 

@@ -266,6 +266,130 @@ int prepare_pair() {
   return (int)cudaFuncSetAttribute(k_irfft2_reg<H, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
+// ------------------------------------------------------------------ rfft2, prefetching variant (64 x 64)
+// Persistent CTAs (one per SM) walk items = (image, 4 channels).  The item's
+// feat rows (4 x 64 rows of 256 bytes) arrive by TMA, 128-byte swizzled, in one
+// of two shared-memory buffers while the previous item is being transformed,
+// so the row pass reads shared memory and the DRAM traffic of one item
+// overlaps the arithmetic and stores of the other.
+//   rows: thread (c, y) = (t / 64, t % 64): the row as a 32-point complex
+//     transform + untangling, into the plane [c][kx][y];
+//   columns: thread (c, h, slot) = (t % 4, t / 4 % 2, t / 8): half h (outputs of
+//     parity h, one DIF stage) of column `slot` (slot 0 = DC + i * Nyquist),
+//     stored to the spectrum, 4 channels = 16 contiguous bytes per store.
+constexpr int PF_CG = 4;
+constexpr uint32_t PF_BOX = 256 * 128;    // one TMA box: 256 rows x 32 floats
+constexpr uint32_t PF_BUF = 2 * PF_BOX;   // one item: x in [0, 32) and [32, 64)
+constexpr int PF_KS = 34, PF_YS = 65;     // plane strides (float2)
+constexpr size_t PF_PLANE = (size_t)PF_CG * PF_KS * PF_YS * sizeof(float2);
+constexpr size_t PF_SMEM = 1024 + 2 * PF_BUF + PF_PLANE + 64;
+
+__global__ void __launch_bounds__(256, 1) k_rfft2_pf(const __grid_constant__ FftPfParams q) {
+  constexpr int H = 64, W = 64, WH = 33, HALF = 32;
+  const FftParams& p = q.p;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float2* plane = reinterpret_cast<float2*>(smem + 2 * PF_BUF);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * PF_BUF + PF_PLANE);
+  auto P = [&](int c, int kx, int y) -> float2& { return plane[(c * PF_KS + kx) * PF_YS + y]; };
+  const int t = threadIdx.x;
+  const int groups = p.c / PF_CG, items = p.batch * groups;
+  auto issue = [&](int item, int s) {
+    const int b = item / groups, c0 = (item - b * groups) * PF_CG;
+    const int row = (b * p.c + c0) * H;
+    const uint32_t bar = smem_u32(full + s);
+    mbar_arrive_expect_tx(bar, PF_BUF);
+    tma_load_2d(smem_u32(smem + s * PF_BUF), &q.feat_map, 0, row, bar);
+    tma_load_2d(smem_u32(smem + s * PF_BUF + PF_BOX), &q.feat_map, 32, row, bar);
+  };
+  if (t == 0) {
+    mbar_init(smem_u32(full), 1);
+    mbar_init(smem_u32(full + 1), 1);
+    fence_mbar_init();
+    tma_prefetch(&q.feat_map);
+  }
+  __syncthreads();
+  if (t == 0) {
+    for (int s = 0; s < 2; s++)
+      if (blockIdx.x + s * gridDim.x < items) issue(blockIdx.x + s * gridDim.x, s);
+  }
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.spec);
+  const int C2 = 2 * p.c;
+  int k = 0;
+  for (int item = blockIdx.x; item < items; item += gridDim.x, k++) {
+    const int s = k & 1;
+    const bool ok = __syncthreads_and(mbar_wait(smem_u32(full + s), (k >> 1) & 1, p.err, 7));
+    if (!ok) break;
+    const int b = item / groups, c0 = (item - b * groups) * PF_CG;
+    {
+      const int c = t >> 6, y = t & 63, r = c * 64 + y;
+      const uint8_t* rowb = smem + s * PF_BUF + r * 128;
+      float2 z[HALF];
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const float4 v = *reinterpret_cast<const float4*>(rowb + (i >> 3) * PF_BOX + (((i & 7) ^ (r & 7)) << 4));
+        z[2 * i] = make_float2(v.x, v.y);
+        z[2 * i + 1] = make_float2(v.z, v.w);
+      }
+      fft_reg<HALF, false>(z);
+#pragma unroll
+      for (int kx = 0; kx <= HALF; kx++) {
+        const float2 zk = z[kx % HALF], zm = conjf2(z[(HALF - kx) % HALF]);
+        const float2 e = make_float2(0.5f * (zk.x + zm.x), 0.5f * (zk.y + zm.y));  // even-sample DFT
+        const float2 d = make_float2(0.5f * (zk.x - zm.x), 0.5f * (zk.y - zm.y));
+        const float2 o = make_float2(d.y, -d.x);                                    // odd-sample DFT = d / i
+        P(c, kx, y) = cadd(e, cmul(o, twid<W, false>(kx)));
+      }
+    }
+    __syncthreads();  // buffer s consumed, plane complete
+    if (t == 0 && item + 2 * gridDim.x < items) {
+      fence_async_smem();
+      issue(item + 2 * gridDim.x, s);
+    }
+    {
+      const int c = t & 3, h = (t >> 2) & 1, slot = t >> 3;
+      float2 u[HALF];
+#pragma unroll
+      for (int n = 0; n < HALF; n++) {
+        float2 a, bb;
+        if (slot == 0) {
+          a = make_float2(P(c, 0, n).x, P(c, HALF, n).x);
+          bb = make_float2(P(c, 0, n + HALF).x, P(c, HALF, n + HALF).x);
+        } else {
+          a = P(c, slot, n);
+          bb = P(c, slot, n + HALF);
+        }
+        u[n] = h ? cmul(csub(a, bb), twid<H, false>(n)) : cadd(a, bb);
+      }
+      fft_reg<HALF, false>(u);  // u[k2] = X[2 k2 + h]
+      const int cc = c0 + c;
+      auto store = [&](int ky, int kx, float2 v) {
+        uint32_t hi, lo;
+        split_pair(v.x * p.scale, v.y * p.scale, hi, lo);
+        const size_t off = (((size_t)b * H + ky) * WH + kx) * C2 + 2 * cc;
+        *reinterpret_cast<uint32_t*>(out + off) = hi;
+        *reinterpret_cast<uint32_t*>(out + p.spec_part + off) = lo;
+      };
+      if (slot == 0) {
+#pragma unroll
+        for (int k2 = 0; k2 < HALF; k2++) {
+          // X[ky] of a + i b and X[-ky] (same parity, this thread)
+          const float2 zk = u[k2];
+          const float2 zm = conjf2(h ? u[HALF - 1 - k2] : u[(HALF - k2) % HALF]);
+          const int ky = 2 * k2 + h;
+          store(ky, 0, make_float2(0.5f * (zk.x + zm.x), 0.5f * (zk.y + zm.y)));
+          const float2 d = make_float2(0.5f * (zk.x - zm.x), 0.5f * (zk.y - zm.y));
+          store(ky, HALF, make_float2(d.y, -d.x));
+        }
+      } else {
+#pragma unroll
+        for (int k2 = 0; k2 < HALF; k2++) store(2 * k2 + h, slot, u[k2]);
+      }
+    }
+    __syncthreads();  // plane free for the next item
+  }
+}
+
 template <int H>
 int dispatch_w(const FftParams& p, bool inv, cudaStream_t st) {
   switch (p.w) {
@@ -287,6 +411,18 @@ int prepare_w() {
 }
 
 }  // namespace
+
+bool fft_pf_supported(int c, int h, int w) { return h == 64 && w == 64 && c % PF_CG == 0; }
+
+int fft_pf_prepare() {
+  return (int)cudaFuncSetAttribute(k_rfft2_pf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
+}
+
+int launch_rfft2_pf(const FftPfParams& q, int grid, cudaStream_t st) {
+  k_rfft2_pf<<<grid, 256, PF_SMEM, st>>>(q);
+  return (int)cudaGetLastError();
+}
+
 
 bool fft_reg_supported(int h, int w) {
   auto ok = [](int n) { return n == 8 || n == 16 || n == 32 || n == 64; };

@@ -219,7 +219,7 @@ def test_spectral_paths_compute_the_same_pass(engine_tamed, oracle_tamed, path):
         engine_tamed.set_spectral_path(0)
 
 
-@pytest.mark.parametrize("h,w,path", [(512, 512, 1), (512, 512, 2), (256, 128, 2), (1024, 1024, 0),
+@pytest.mark.parametrize("h,w,path", [(512, 512, 1), (512, 512, 2), (512, 512, 3), (256, 128, 2), (1024, 1024, 0),
                                       (2048, 2048, 0), (600, 600, 0), (520, 776, 0)])
 def test_spectral_kernels_on_large_latents(engine_tamed, h, w, path):
     """rfft2 and irfft2 (+ the FourierUnit residual) of the first resblock at
@@ -277,3 +277,19 @@ def test_a_device_wait_that_runs_out_is_reported_and_the_engine_recovers(engine_
     assert ei.value.code == -4 and "timed out" in ei.value.msg and "code 6" in ei.value.msg
     _, _, x = make_input(64, 64, 91)
     assert np.abs(engine_tamed.forward(x) - oracle_tamed.forward(x)).max() <= FLOAT_TOL
+
+
+def test_prefetching_rfft_matches_the_register_path_over_a_batch(engine_tamed):
+    """The persistent prefetching rfft2 (64x64 planes) walks several items per
+    CTA through its two TMA buffers once the batch has more than one item per
+    SM (4 images x 48 channel groups); the pass must match the register path."""
+    xs = np.stack([make_input(512, 512, s)[2] for s in (95, 96, 97, 98)])
+    try:
+        engine_tamed.set_spectral_path(engine_tamed.SPECTRAL_REGISTER)
+        ref = engine_tamed.forward(xs)
+        engine_tamed.set_spectral_path(engine_tamed.SPECTRAL_PREFETCH)
+        got = engine_tamed.forward(xs)
+        np.testing.assert_array_equal(got, engine_tamed.forward(xs))  # deterministic
+    finally:
+        engine_tamed.set_spectral_path(engine_tamed.SPECTRAL_AUTO)
+    assert np.abs(got - ref).max() <= FLOAT_TOL
