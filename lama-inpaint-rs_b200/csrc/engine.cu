@@ -473,7 +473,7 @@ void load_weights(const WeightFile& wf, Weights& W) {
 }
 
 // ------------------------------------------------------------------ ops
-enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
+enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_IRFFT_PAR, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
 
 struct Op {
   OpKind kind;
@@ -503,6 +503,7 @@ int launch_op(const Op& op, cudaStream_t st) {
     case OP_RFFT_REG: return launch_fft_reg(op.f, false, st);
     case OP_IRFFT_REG: return launch_fft_reg(op.f, true, st);
     case OP_RFFT_PF: return launch_rfft2_pf(*op.fpf, op.grid, st);
+    case OP_IRFFT_PAR: return launch_irfft2_par(op.f, st);
     case OP_UNFOLD_F32: return launch_unfold_f32(op.u, st);
     case OP_UNFOLD_U8: return launch_unfold_u8(op.u, st);
     case OP_COMPOSITE: return launch_composite(op.c, st);
@@ -883,7 +884,7 @@ struct Builder {
         gemm("fourier_conv", F.fu, {{spec, 1, false}}, {one_seg(0, 0, 384, SegSpec{0, 0, 384, 1, {{0, 0}}})}, 64, B, 1, h * wh,
              OutSpec{OUT_F32_NHWC, fu, 0, 384, 1, h * wh, 0, 0, nullptr}, 1, 0, 2.0 * pxs * 384 * 384);
         Op ir;
-        ir.kind = reg ? OP_IRFFT_REG : OP_IRFFT;
+        ir.kind = pf ? OP_IRFFT_PAR : reg ? OP_IRFFT_REG : OP_IRFFT;
         ir.name = "irfft2";
         ir.f = fp;
         ir.bytes = pxs * 384 * 4 + px * 192 * 4 + px * 192 * 4;

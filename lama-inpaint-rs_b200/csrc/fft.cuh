@@ -87,6 +87,9 @@ bool fft_reg_supported(int h, int w);
 bool fft_pf_supported(int c, int h, int w);
 int fft_pf_prepare();
 int launch_rfft2_pf(const FftPfParams& q, int grid, cudaStream_t st);
+// irfft2 of 64 x 64 planes split by output-row parity, 16 channels per CTA
+// (fft_reg.cu); needs c % 16 == 0.
+int launch_irfft2_par(const FftParams& p, cudaStream_t st);
 int fft_reg_prepare();
 int launch_fft_reg(const FftParams& p, bool inverse, cudaStream_t st);
 

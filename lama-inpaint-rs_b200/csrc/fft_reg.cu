@@ -390,6 +390,95 @@ __global__ void __launch_bounds__(256, 1) k_rfft2_pf(const __grid_constant__ Fft
   }
 }
 
+// ------------------------------------------------------------------ irfft2 by row parity (64 x 64)
+// One CTA = one image x 16 channels x one parity h of the output rows: the
+// column pass computes only the outputs y = 2m + h of every inverse column
+// transform (one decimation-in-frequency stage, then 32 points in
+// registers), so the half plane [16][kx][32] fits in shared memory and the
+// row pass stores S with 16 channels = 32 contiguous bytes per pixel and part.
+constexpr int PAR_CG = 16, PAR_KS = 34, PAR_YS = 33;
+constexpr size_t PAR_SMEM = (size_t)PAR_CG * PAR_KS * PAR_YS * sizeof(float2);
+
+__global__ void __launch_bounds__(256, 1) k_irfft2_par(const FftParams p) {
+  constexpr int H = 64, W = 64, WH = 33, HALF = 32;
+  extern __shared__ __align__(16) float2 zp[];
+  auto P = [&](int c, int kx, int m) -> float2& { return zp[(c * PAR_KS + kx) * PAR_YS + m]; };
+  const int t = threadIdx.x, h = blockIdx.z, b = blockIdx.y, c0 = blockIdx.x * PAR_CG;
+  const int c = t & 15, cc = c0 + c;
+  const int C2 = 2 * p.c;
+  auto ld = [&](int ky, int kx) {
+    return __ldg(reinterpret_cast<const float2*>(p.fu + (((size_t)b * H + ky) * WH + kx) * C2 + 2 * cc));
+  };
+  // Hermitian parts of the DC and Nyquist columns, h(k) = (v(k) + conj(v(-k))) / 2,
+  // packed as z = h0 + i * hn
+  auto packed = [&](int ky) {
+    const int km = (H - ky) % H;
+    const float2 a0 = ld(ky, 0), a0m = ld(km, 0), an = ld(ky, HALF), anm = ld(km, HALF);
+    const float2 h0 = make_float2(0.5f * (a0.x + a0m.x), 0.5f * (a0.y - a0m.y));
+    const float2 hn = make_float2(0.5f * (an.x + anm.x), 0.5f * (an.y - anm.y));
+    return make_float2(h0.x - hn.y, h0.y + hn.x);
+  };
+#pragma unroll 1
+  for (int slot = t >> 4; slot < HALF; slot += 16) {
+    float2 u[HALF];
+    if (slot == 0) {
+#pragma unroll
+      for (int n = 0; n < HALF; n++) {
+        const float2 a = packed(n), bb = packed(n + HALF);
+        u[n] = h ? cmul(csub(a, bb), twid<H, true>(n)) : cadd(a, bb);
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < HALF; n++) {
+        const float2 a = ld(n, slot), bb = ld(n + HALF, slot);
+        u[n] = h ? cmul(csub(a, bb), twid<H, true>(n)) : cadd(a, bb);
+      }
+    }
+    fft_reg<HALF, true>(u);  // u[m] = y[2m + h]
+    if (slot == 0) {
+#pragma unroll
+      for (int m = 0; m < HALF; m++) {
+        P(c, 0, m) = make_float2(u[m].x, 0.f);
+        P(c, HALF, m) = make_float2(u[m].y, 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < HALF; m++) P(c, slot, m) = u[m];
+    }
+  }
+  __syncthreads();
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.s_out);
+#pragma unroll 1
+  for (int m = t >> 4; m < HALF; m += 16) {
+    const int y = 2 * m + h;
+    float2 z[HALF];
+#pragma unroll
+    for (int kx = 0; kx < HALF; kx++) {
+      const float2 xk = P(c, kx, m);
+      const float2 xm = conjf2(P(c, HALF - kx, m));
+      const float2 e = cadd(xk, xm);                           // X[k] + X[k+W/2]
+      const float2 o = cmul(csub(xk, xm), twid<W, true>(kx));  // (X[k] - X[k+W/2]) e^{+2 pi i k/W}
+      z[kx] = make_float2(e.x - o.y, e.y + o.x);               // e + i*o
+    }
+    fft_reg<HALF, true>(z);
+    const float4* fr = reinterpret_cast<const float4*>(p.feat + (((size_t)b * p.c + cc) * H + y) * W);
+    __nv_bfloat16* o = out + ((size_t)b * H + y) * W * p.c + cc;
+#pragma unroll
+    for (int i = 0; i < W / 4; i++) {
+      const float4 f = __ldg(fr + i);
+      const float v[4] = {z[2 * i].x * p.scale + f.x, z[2 * i].y * p.scale + f.y,
+                          z[2 * i + 1].x * p.scale + f.z, z[2 * i + 1].y * p.scale + f.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const __nv_bfloat16 hv = __float2bfloat16_rn(v[j]);
+        const size_t off = (size_t)(4 * i + j) * p.c;
+        o[off] = hv;
+        o[p.s_part + off] = __float2bfloat16_rn(v[j] - __bfloat162float(hv));
+      }
+    }
+  }
+}
+
 template <int H>
 int dispatch_w(const FftParams& p, bool inv, cudaStream_t st) {
   switch (p.w) {
@@ -415,7 +504,14 @@ int prepare_w() {
 bool fft_pf_supported(int c, int h, int w) { return h == 64 && w == 64 && c % PF_CG == 0; }
 
 int fft_pf_prepare() {
-  return (int)cudaFuncSetAttribute(k_rfft2_pf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
+  cudaError_t e = cudaFuncSetAttribute(k_rfft2_pf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
+  if (e != cudaSuccess) return (int)e;
+  return (int)cudaFuncSetAttribute(k_irfft2_par, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PAR_SMEM);
+}
+
+int launch_irfft2_par(const FftParams& p, cudaStream_t st) {
+  k_irfft2_par<<<dim3(p.c / PAR_CG, p.batch, 2), 256, PAR_SMEM, st>>>(p);
+  return (int)cudaGetLastError();
 }
 
 int launch_rfft2_pf(const FftPfParams& q, int grid, cudaStream_t st) {
