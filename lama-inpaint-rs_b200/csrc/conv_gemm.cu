@@ -38,8 +38,8 @@ __host__ __device__ constexpr int stages_for(int bn) {
   // (2 * A_PART + 2 * bn * 128) bytes per stage, within ~200 KB
   return bn <= 16 ? 5 : bn <= 64 ? 4 : bn <= 128 ? 3 : 2;
 }
-// Extra shared memory of the shifted-sum epilogue (OUT_SHIFT7_NCHW):
-// two 128 x 33 fp32 staging tiles.
+// Swapped tiles transpose through 32 x 33 fp32 staging tiles (one per
+// epilogue warp).
 constexpr int SHIFT_LD = 33;
 // Tile widths whose split outputs can leave through TMA stores: each of the
 // 8 epilogue warps stages 32 pixels x 32 channels (hi and lo, 2 KB each) at
@@ -48,8 +48,7 @@ __host__ __device__ constexpr bool tma_store_bn(int bn) { return bn == 64 || bn 
 constexpr uint32_t STAGING_OFF = 1024;
 constexpr uint32_t STAGING_WARP = 4096;
 __host__ __device__ constexpr uint32_t extra_smem(int bn) {
-  return bn == 32 ? 2u * 128u * SHIFT_LD * 4u
-                  : bn == 256 ? 8u * 32u * SHIFT_LD * 4u : tma_store_bn(bn) ? STAGING_OFF - 256u + 8u * STAGING_WARP : 0u;
+  return bn == 256 ? 8u * 32u * SHIFT_LD * 4u : tma_store_bn(bn) ? STAGING_OFF - 256u + 8u * STAGING_WARP : 0u;
 }
 __host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 2 * A_PART + 2u * (uint32_t)bn * 128u; }
 __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
@@ -87,7 +86,7 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t, int 
   ti.b = mt / per_img;
   int r = mt - ti.b * per_img;
   ti.i0 = (r / p.tiles_x) * p.bh;
-  ti.j0 = (r % p.tiles_x) * p.step_x;
+  ti.j0 = (r % p.tiles_x) * p.bw;
   return ti;
 }
 
@@ -563,36 +562,6 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       const int i = ti.i0 + m / p.bw, j = ti.j0 + m % p.bw;
       const bool valid = (i < p.mh) && (j < p.mw) && !ti.dummy;
       const int oy = i * C.oy_mul + C.oy_add, ox = j * C.ox_mul + C.ox_add;
-      if constexpr (BN == 32) {
-        if (p.out_kind == OUT_SHIFT7_NCHW) {
-          if (half) {  // one 32-column chunk: the first four epilogue warps take it
-            release(acc);
-            continue;
-          }
-          float v[32];
-          tmem_ld32(trow, v);
-          tmem_wait_ld();
-          float* P = shift_buf + (it & 1) * 128 * SHIFT_LD;
-#pragma unroll
-          for (int k = 0; k < 32; k++) P[m * SHIFT_LD + k] = v[k];
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          const int x = ti.j0 + m;
-          if (m < p.step_x && x < p.out_w && i < p.mh) {
-#pragma unroll
-            for (int co = 0; co < 3; co++) {
-              float acc = 0.f;
-#pragma unroll
-              for (int kx = 0; kx < 7; kx++) acc += P[(m + kx) * SHIFT_LD + kx * 4 + co];
-              const float z = acc + __ldg(p.shift + co);
-              const float e = expf(-z);
-              reinterpret_cast<float*>(p.out)[(((long long)ti.b * p.out_c + co) * p.out_h + i) * p.out_w + x] =
-                  1.0f / (1.0f + e);
-            }
-          }
-          release(acc);
-          continue;
-        }
-      }
       // split-K: every part stores its raw sums in its own workspace slice; the
       // CTA whose part arrives last finishes the tile from the sum of the
       // slices in part order (deterministic), the others are done

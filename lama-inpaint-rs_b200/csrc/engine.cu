@@ -33,6 +33,7 @@
 #include "fft.cuh"
 #include "gemm.cuh"
 #include "lama_b200.h"
+#include "outconv.cuh"
 #include "pointwise.cuh"
 #include "ptx.cuh"
 #include "weights.h"
@@ -453,19 +454,18 @@ void load_weights(const WeightFile& wf, Weights& W) {
     for (int n = 0; n < cout; n++) t[n] = bias[n] * s[n] + t[n];
     L.affine(W.ct[u], s, t);
   }
-  // OutConv 7x7 64 -> 3 with bias, over the reflect-padded input.  The seven
-  // x taps go into N (n = kx*4 + co, 28 used of 32) and K = (ky, c) = 448;
-  // the epilogue sums the kx partial products across neighbouring pixels.
+  // OutConv 7x7 64 -> 3 with bias, over the reflect-padded input, for the
+  // row-ring kernel (outconv.cu): n = ky*21 + kx*3 + co (147 of 160), K = c.
   {
     auto w = L.get("model.34.weight", {3, 64, 7, 7});
     auto bias = L.get("model.34.bias", {3});
-    std::vector<float> m((size_t)32 * 448, 0.f);
-    for (int kx = 0; kx < 7; kx++)
-      for (int co = 0; co < 3; co++)
-        for (int ky = 0; ky < 7; ky++)
+    std::vector<float> m2((size_t)160 * 64, 0.f);
+    for (int ky = 0; ky < 7; ky++)
+      for (int kx = 0; kx < 7; kx++)
+        for (int co = 0; co < 3; co++)
           for (int c = 0; c < 64; c++)
-            m[(size_t)(kx * 4 + co) * 448 + ky * 64 + c] = w[(((size_t)co * 64 + c) * 7 + ky) * 7 + kx];
-    W.outc.cls.push_back(L.upload(m, 32, 448));
+            m2[(size_t)(ky * 21 + kx * 3 + co) * 64 + c] = w[(((size_t)co * 64 + c) * 7 + ky) * 7 + kx];
+    W.outc.cls.push_back(L.upload(m2, 160, 64));
     std::vector<float> one(32, 1.f), sh(32, 0.f);
     for (int n = 0; n < 3; n++) sh[n] = bias[n];
     L.affine(W.outc, one, sh);
@@ -473,7 +473,7 @@ void load_weights(const WeightFile& wf, Weights& W) {
 }
 
 // ------------------------------------------------------------------ ops
-enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_IRFFT_PAR, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
+enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_IRFFT_PAR, OP_OUTCONV, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
 
 struct Op {
   OpKind kind;
@@ -481,6 +481,7 @@ struct Op {
   int bn = 0, grid = 0;
   std::unique_ptr<GemmParams> g;
   std::unique_ptr<FftPfParams> fpf;
+  std::unique_ptr<OutConvParams> oc;
   FftParams f{};
   UnfoldParams u{};
   CompositeParams c{};
@@ -504,6 +505,7 @@ int launch_op(const Op& op, cudaStream_t st) {
     case OP_IRFFT_REG: return launch_fft_reg(op.f, true, st);
     case OP_RFFT_PF: return launch_rfft2_pf(*op.fpf, op.grid, st);
     case OP_IRFFT_PAR: return launch_irfft2_par(op.f, st);
+    case OP_OUTCONV: return launch_outconv(*op.oc, op.grid, st);
     case OP_UNFOLD_F32: return launch_unfold_f32(op.u, st);
     case OP_UNFOLD_U8: return launch_unfold_u8(op.u, st);
     case OP_COMPOSITE: return launch_composite(op.c, st);
@@ -628,7 +630,7 @@ struct Builder {
 
   void gemm(const std::string& name, const GemmW& Wt, const std::vector<AmapSpec>& amaps,
             const std::vector<ClassSpec>& classes, int cb, int B, int mh, int mw, const OutSpec& o, int relu,
-            int sigmoid, double flops, int force_bn = 0, int step_x = 0, bool allow_swap = true) {
+            int sigmoid, double flops) {
     Op op;
     op.kind = OP_GEMM;
     op.name = name;
@@ -643,7 +645,7 @@ struct Builder {
     // since split outputs leave through TMA stores (pixel-major tiles only),
     // pixel-major tiles beat swapped ones for the FFC layers at batch 1 and 32
     // and for the FourierUnit conv, so only LAMA_TILING_SWAPPED selects them.
-    bool swap = allow_swap && e.tiling == LAMA_TILING_SWAPPED && step_x == 0 && force_bn == 0 && cb == 64 &&
+    bool swap = e.tiling == LAMA_TILING_SWAPPED && cb == 64 &&
                 (o.kind == OUT_SPLIT || o.kind == OUT_F32_NHWC);
     for (auto& c : classes) swap = swap && c.nvalid % 128 == 0;
     int bh = 1, bw = 128;
@@ -653,7 +655,7 @@ struct Builder {
     if (!swap) {
       bh = 1;
       bw = 128;
-      if (step_x == 0) choose_tile(mh, mw, bh, bw, 128, max_stride);
+      choose_tile(mh, mw, bh, bw, 128, max_stride);
     }
     p.swap = swap ? 1 : 0;
     p.cb = cb;
@@ -662,13 +664,12 @@ struct Builder {
     p.mw = mw;
     p.bh = bh;
     p.bw = bw;
-    p.step_x = step_x ? step_x : bw;
     p.tiles_y = (mh + bh - 1) / bh;
-    p.tiles_x = (mw + p.step_x - 1) / p.step_x;
+    p.tiles_x = (mw + bw - 1) / bw;
     p.m_tiles = B * p.tiles_y * p.tiles_x;
     std::vector<int> ns;
     for (auto& c : classes) ns.push_back(c.nvalid);
-    const int bn = swap ? 256 : force_bn ? force_bn : choose_bn(ns, p.m_tiles);
+    const int bn = swap ? 256 : choose_bn(ns, p.m_tiles);
     if (!bn) throw EngineError{LAMA_EUNSUPPORTED, name + ": no tile width divides the output channels"};
     op.bn = bn;
     // CTA pairs (256 x BN tiles over two SMs) where the kernel has them and
@@ -714,12 +715,11 @@ struct Builder {
     }
     // Split-K for launches too small to fill the GPU (batch-1 passes): K parts
     // of at most ~the per-SM share of all K blocks, finished in-kernel by the
-    // last part (pixel-major single-CTA tiles, 32-column chunks, not the
-    // shifted-sum OutConv).
+    // last part (pixel-major single-CTA tiles, 32-column chunks).
     long long kbs = 0;
     for (size_t ci = 0; ci < classes.size(); ci++) kbs += (long long)p.m_tiles * p.cls[ci].ntiles_n * p.cls[ci].nkb;
     const int share = (int)std::max<long long>(12, (kbs + e.sms - 1) / e.sms);
-    const bool can_split = !swap && !pair && bn >= 32 && o.kind != OUT_SHIFT7_NCHW && p.step_x == bw;
+    const bool can_split = !swap && !pair && bn >= 32;
     int ws_tiles = 0;
     for (size_t ci = 0; ci < classes.size(); ci++) {
       GemmClass& C = p.cls[ci];
@@ -758,7 +758,7 @@ struct Builder {
       aligned = aligned && c.n0 % 32 == 0;
       dense = dense && c.oy_mul == 1 && c.ox_mul == 1 && c.oy_add == 0 && c.ox_add == 0;
     }
-    if (!swap && (bn == 64 || bn == 128 || bn == 192) && aligned && p.step_x == bw &&
+    if (!swap && (bn == 64 || bn == 128 || bn == 192) && aligned &&
         (bw >= 32 ? bw % 32 == 0 : 32 % bw == 0)) {
       if (o.kind == OUT_SPLIT) {
         for (size_t ci = 0; ci < classes.size(); ci++) {
@@ -778,7 +778,7 @@ struct Builder {
     op.out_ptr = o.p;
     op.out_split = o.kind == OUT_SPLIT;
     op.out_part = o.part;
-    if (o.kind == OUT_F32_NCHW || o.kind == OUT_SHIFT7_NCHW) {
+    if (o.kind == OUT_F32_NCHW) {
       op.dims[0] = B; op.dims[1] = o.c; op.dims[2] = o.h; op.dims[3] = o.w;
     } else {
       op.dims[0] = B; op.dims[1] = o.h + 2 * o.halo; op.dims[2] = o.w + 2 * o.halo; op.dims[3] = o.c;
@@ -962,13 +962,29 @@ struct Builder {
            2.0 * B * in.H * in.W * cout * in.C * 9);
     }
     // OutConv 7x7 64 -> 3 over the reflect-pad-3 halo, + bias, sigmoid -> fp32 NCHW:
-    // 7 row taps x 64 channels, N = (kx, co); 128-pixel row tiles stepping 122
-    // so every output's seven column partials sit in one tile
+    // all 147 tap products of each input row at once, summed in a ring of
+    // output rows (outconv.cu), every input row read once
     {
-      std::vector<std::pair<int, int>> t;
-      for (int ky = 0; ky < 7; ky++) t.push_back({ky, 0});
-      gemm("outconv_7x7", e.W.outc, {{U3, 1, false}}, {one_seg(0, 0, 32, SegSpec{0, 0, 64, 1, t})}, 64, B, H, W,
-           OutSpec{OUT_SHIFT7_NCHW, out, 0, 3, H, W, 0, 0, nullptr}, 0, 1, 2.0 * B * H * W * 3 * 3136, 32, 122);
+      Op op;
+      op.kind = OP_OUTCONV;
+      op.name = "outconv_7x7";
+      op.flops = 2.0 * B * H * W * 3 * 3136;
+      op.oc.reset(new OutConvParams());
+      OutConvParams& q = *op.oc;
+      q.amap = act_map(U3, 64, 128, 1, 1, false);
+      q.wmap = w_map(e.W.outc.cls[0], 160);
+      q.bias = e.W.outc.shift;
+      q.out = out;
+      q.batch = B;
+      q.h = H;
+      q.w = W;
+      q.err = e.d_err;
+      outconv_units(q, e.sms);
+      op.grid = e.sms;
+      op.out_ptr = out;
+      op.out_split = 0;
+      op.dims[0] = B; op.dims[1] = 3; op.dims[2] = H; op.dims[3] = W;
+      pl.ops.push_back(std::move(op));
     }
   }
 };
@@ -1144,6 +1160,7 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
     CKL(fft_prepare(kFftSmem));
     CKL(fft_reg_prepare());
     CKL(fft_pf_prepare());
+    CKL(outconv_prepare());
     e->d_err = (int*)e->wmem.alloc(256);
     upload_weights(e->W, e->wmem);
   } catch (const EngineError& x) {

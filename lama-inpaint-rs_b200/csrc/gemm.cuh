@@ -33,11 +33,6 @@ enum OutKind : int {
   OUT_SPLIT = 0,     // split bf16 NHWC (optionally halo'd, reflect-filled)
   OUT_F32_NHWC = 1,  // fp32 NHWC
   OUT_F32_NCHW = 2,  // fp32 NCHW, channels < nvalid only
-  // 7x7 conv with the x taps folded into N (n = kx*4 + co): the epilogue sums
-  // acc[m + kx][kx*4 + co] over kx across the tile's pixels, adds the bias
-  // (shift[co]), applies the sigmoid and stores fp32 NCHW.  Tiles are 128
-  // pixels of one row stepping `step_x` = 122 columns.  BN = 32 only.
-  OUT_SHIFT7_NCHW = 3,
 };
 
 struct GemmSeg {
@@ -86,7 +81,6 @@ struct GemmParams {
   int batch, mh, mw;          // M space: images x rows x cols
   int bh, bw;                 // tile rows x cols, bh * bw == 128
   int tiles_y, tiles_x, m_tiles;
-  int step_x;                 // column step between tiles (== bw unless overlapping)
   int total_tiles;
   // epilogue
   const float* scale;         // per absolute output channel

@@ -1,0 +1,23 @@
+// OutConv 7x7 64 -> 3 + bias + sigmoid with every input row read once (outconv.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace lama {
+
+struct OutConvParams {
+  CUtensorMap amap;   // input: split bf16 (64, W + 6, H + 6, B, part), boxes of 64 x 128 x 1, 128B swizzle
+  CUtensorMap wmap;   // weights: split bf16 [2][160][64], n = ky * 21 + kx * 3 + co, boxes of 64 x 160
+  const float* bias;  // [3]
+  float* out;         // [B][3][H][W] fp32
+  int batch, h, w;
+  int strips, segs, seg;  // filled by outconv_units (seg = output rows per segment)
+  int* err;           // device status word
+};
+
+int outconv_prepare();
+void outconv_units(OutConvParams& q, int sms);
+int launch_outconv(const OutConvParams& q, int sms, cudaStream_t st);
+
+}  // namespace lama
