@@ -971,7 +971,7 @@ struct Builder {
       op.flops = 2.0 * B * H * W * 3 * 3136;
       op.oc.reset(new OutConvParams());
       OutConvParams& q = *op.oc;
-      q.amap = act_map(U3, 64, 128, 1, 1, false);
+      q.amap = act_map(U3, 64, 32, 1, 1, false);  // 32-column boxes, four per row and part
       q.wmap = w_map(e.W.outc.cls[0], 160);
       q.bias = e.W.outc.shift;
       q.out = out;

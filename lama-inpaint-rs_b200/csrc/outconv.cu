@@ -6,22 +6,25 @@
 // of a strip, all 147 tap products P[px][n], n = ky*21 + kx*3 + co (N = 160,
 // K = the 64 input channels, three BF16 MMAs of split operands).  Output
 // pixel (y, x) of channel co is the sum over (ky, kx) of P of input row
-// y + ky at column x + kx: the epilogue stages P in shared memory, each
-// thread (one output column) sums the seven kx products per (ky, co) and adds
-// them into a ring of seven output-row accumulators in registers; output row
-// r - 6 is complete after input row r and is stored (sigmoid, fp32 NCHW).
+// y + ky at column x + kx.  TMEM lane = input column: the 128 rows of A are
+// four groups of 32 input columns that start 26 columns apart, so lane l < 26
+// of a warp finds the inputs x .. x + 6 of its output column x in its own
+// warp and takes P[x + kx][*] from the lane kx places up (warp shuffles).
+// The kx sums go into a ring of seven output-row accumulators in registers;
+// output row r - 6 is complete after input row r and is stored (sigmoid,
+// fp32 NCHW).
 //
-// Work units are (image, strip of 122 output columns = 128 input columns,
-// segment of up to 64 output rows, read with 6 extra input rows; shorter
-// segments when a batch has too few units for the SMs).  Warp 0 issues the
-// TMA loads (one 128 x 64 box per row and part, weights once), warp 1 the
-// MMAs into a double-buffered TMEM accumulator, warp 2 owns TMEM, warps 4..11
-// are the epilogue: warps 4+q and 8+q drain TMEM lanes 32q.. (input columns)
-// in two column halves; then thread (column, part) sums ky 0..3 (part 0) or
-// 4..6 (part 1) into its ring, and part 0 adds part 1's sums when a row is
-// complete.
+// Work units are (image, strip of 104 output columns, segment of 16..64
+// output rows, read with 6 extra input rows).  Warp 0 issues the TMA loads
+// (four 32 x 64 boxes per row and part, weights once),
+// warp 1 the MMAs into a double-buffered TMEM accumulator, warp 2 owns TMEM,
+// warps 4..11 are the epilogue: warps 4+q (part 0, ky 0..3) and 8+q (part 1,
+// ky 4..6) read TMEM lanes 32q.. and keep their own rings; part 1 hands its
+// sums of a completed row to part 0 (through a buffer per row parity, one
+// named barrier per row), which adds the bias and stores.
 #include <algorithm>
 #include <cstdint>
+#include <type_traits>
 
 #include "outconv.cuh"
 #include "ptx.cuh"
@@ -30,22 +33,21 @@ namespace lama {
 namespace {
 
 constexpr int OC_N = 160;                    // 147 products, padded to a multiple of 16
-constexpr int OC_NST = 3;                    // A stages
+constexpr int OC_NST = 5;                    // A stages
 constexpr uint32_t OC_A = 128 * 64 * 2;      // one part of one input-row tile
 constexpr uint32_t OC_STAGE = 2 * OC_A;      // hi + lo
 constexpr uint32_t OC_WPART = OC_N * 64 * 2;  // one part of the weights
-constexpr int OC_PLD = 161;                  // P row stride (floats)
-constexpr uint32_t OC_P_OFF = OC_NST * OC_STAGE + 2 * OC_WPART;
-constexpr uint32_t OC_X_OFF = OC_P_OFF + 128 * OC_PLD * 4;  // [128][3] partial sums of ky 4..6
-constexpr uint32_t OC_BAR_OFF = OC_X_OFF + 128 * 3 * 4;
+// [2][128][3]: part 1's sums of ky 4..6 for a completed row, by row parity
+constexpr uint32_t OC_X_OFF = OC_NST * OC_STAGE + 2 * OC_WPART;
+constexpr uint32_t OC_BAR_OFF = OC_X_OFF + 2 * 128 * 3 * 4;
 constexpr size_t OC_SMEM = 1024 + OC_BAR_OFF + 256;
-constexpr int OC_STRIP = 122, OC_SEG_MAX = 64;
+constexpr int OC_QCOLS = 26;                 // output columns of a warp (32 input columns)
+constexpr int OC_STRIP = 4 * OC_QCOLS, OC_SEG_MAX = 64;
 
 __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__ OutConvParams q) {
   constexpr uint32_t IDESC = idesc_bf16_f32(OC_N);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* P = reinterpret_cast<float*>(smem + OC_P_OFF);
   float* X = reinterpret_cast<float*>(smem + OC_X_OFF);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OC_BAR_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * OC_NST + 5);
@@ -109,8 +111,12 @@ __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__
           if (!mbar_wait(empty_bar(stage), phase ^ 1, q.err, 11)) { ok = false; break; }
           mbar_arrive_expect_tx(full_bar(stage), OC_STAGE);
           const uint32_t sa = smem0 + stage * OC_STAGE;
-          tma_load_5d(sa, &q.amap, 0, x0, y0 + rr, b, 0, full_bar(stage));
-          tma_load_5d(sa + OC_A, &q.amap, 0, x0, y0 + rr, b, 1, full_bar(stage));
+#pragma unroll
+          for (int part = 0; part < 2; part++)
+#pragma unroll
+            for (int g = 0; g < 4; g++)  // A rows 32g.. = input columns x0 + 26g ..
+              tma_load_5d(sa + part * OC_A + g * 4096, &q.amap, 0, x0 + g * OC_QCOLS, y0 + rr, b, part,
+                          full_bar(stage));
           if (++stage == OC_NST) { stage = 0; phase ^= 1; }
         }
       }
@@ -149,10 +155,9 @@ __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__
       }
     }
   } else if (warp >= 4) {
-    const int quarter = (warp - 4) & 3, half = (warp - 4) >> 2;
-    const int tp = threadIdx.x - 128;
-    const int px = tp & 127, part = tp >> 7;    // reduction role: input column, ky group
-    const int lp = quarter * 32 + lane;         // TMEM lane = input column of the drain role
+    const int quarter = (warp - 4) & 3, part = (warp - 4) >> 2;
+    const int px = quarter * 32 + lane;        // TMEM lane
+    const int ox = quarter * OC_QCOLS + lane;  // strip column: input column of the lane, output column if lane < 26
     const float bias0 = __ldg(q.bias), bias1 = __ldg(q.bias + 1), bias2 = __ldg(q.bias + 2);
     // Every epilogue thread passes the same named barriers the same number of
     // times, also after a bounded wait has run out (then it only takes part
@@ -163,8 +168,8 @@ __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__
       int b, x0, y0, nout;
       decode(u, b, x0, y0, nout);
       const int nin = nout + 6;
-      const bool col = px < OC_STRIP && x0 + px < q.w;
-      float* ob = q.out + (size_t)b * 3 * q.h * q.w + (size_t)y0 * q.w + x0 + px;
+      const bool col = lane < OC_QCOLS && x0 + ox < q.w;
+      float* ob = q.out + (size_t)b * 3 * q.h * q.w + (size_t)y0 * q.w + x0 + ox;
       float acc[7][3];
 #pragma unroll
       for (int s = 0; s < 7; s++) acc[s][0] = acc[s][1] = acc[s][2] = 0.f;
@@ -175,65 +180,75 @@ __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__
           if (rr >= nin) break;
           const int a = it & 1;
           if (ok) ok = mbar_wait(tfull_bar(a), (it >> 1) & 1, q.err, 15);
+          ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the shuffles below take every lane
           it++;
           tc_fence_after();
+          // part 0: columns 0..95 (ky 0..3 = n 0..83); part 1: columns 64..159
+          // (ky 4..6 = n 84..146 at v[20..82])
+          float v[96];
           if (ok) {
-            // drain: columns [80 * half, 80 * half + 80) of TMEM lane lp into P
-            const uint32_t trow = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * OC_N + half * 80);
-            float* prow = P + lp * OC_PLD + half * 80;
-            float v[32];
+            const uint32_t trow = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * OC_N + part * 64);
             tmem_ld32(trow, v);
+            tmem_ld32(trow + 32, v + 32);
+            tmem_ld32(trow + 64, v + 64);
             tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; j++) prow[j] = v[j];
-            tmem_ld32(trow + 32, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; j++) prow[32 + j] = v[j];
-            tmem_ld16(trow + 64, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; j++) prow[64 + j] = v[j];
           }
           tc_fence_before();
           if (ok) mbar_arrive(tempty_bar(a));
-          asm volatile("bar.sync 1, 256;" ::: "memory");
-          if (ok && col) {
+          if (ok) {
             // input row rr feeds output rows rr - ky (ring slot (i - ky) mod 7)
+            auto tap_sums = [&](auto part_c) {
+              constexpr int P1 = decltype(part_c)::value;
+              constexpr int KY0 = P1 ? 4 : 0, KY1 = P1 ? 7 : 4, VOFF = P1 ? 64 : 0;
 #pragma unroll
-            for (int ky = 0; ky < 7; ky++) {
-              if ((ky < 4) != (part == 0)) continue;
-              const int yy = rr - ky;
-              if (yy < 0 || yy >= nout) continue;
-              float t0 = 0.f, t1 = 0.f, t2 = 0.f;
+              for (int ky = KY0; ky < KY1; ky++) {
+                const int yy = rr - ky;
+                const bool live = yy >= 0 && yy < nout;
+                float t[3];
 #pragma unroll
-              for (int kx = 0; kx < 7; kx++) {
-                const float* pp = P + (px + kx) * OC_PLD + ky * 21 + kx * 3;
-                t0 += pp[0];
-                t1 += pp[1];
-                t2 += pp[2];
+                for (int co = 0; co < 3; co++) {
+                  t[co] = v[ky * 21 + co - VOFF];
+#pragma unroll
+                  for (int kx = 1; kx < 7; kx++) {
+                    const int n = ky * 21 + kx * 3 + co;
+                    t[co] += __shfl_down_sync(0xffffffffu, v[n - VOFF], kx);
+                  }
+                }
+                if (live) {
+                  float* s = acc[(i - ky + 7) % 7];
+                  s[0] += t[0];
+                  s[1] += t[1];
+                  s[2] += t[2];
+                }
               }
-              float* s = acc[(i - ky + 7) % 7];
-              s[0] += t0;
-              s[1] += t1;
-              s[2] += t2;
-            }
+            };
+            if (part == 0) tap_sums(std::integral_constant<int, 0>{});
+            else tap_sums(std::integral_constant<int, 1>{});
             if (part == 1 && rr >= 6) {  // hand the completed row's ky 4..6 sums to part 0
               float* s = acc[(i + 1) % 7];
-              X[px * 3] = s[0];
-              X[px * 3 + 1] = s[1];
-              X[px * 3 + 2] = s[2];
+              if (col) {
+                float* xs = X + a * 384 + px * 3;
+                xs[0] = s[0];
+                xs[1] = s[1];
+                xs[2] = s[2];
+              }
               s[0] = s[1] = s[2] = 0.f;
             }
           }
+          // X[a] written above is read below; X[a] is written again two rows
+          // later, after every part-0 thread has passed the next barrier
           asm volatile("bar.sync 1, 256;" ::: "memory");
           // output row rr - 6 is complete
-          if (ok && col && part == 0 && rr >= 6) {
+          if (ok && part == 0 && rr >= 6) {
             float* s = acc[(i + 1) % 7];
-            const int yd = rr - 6;
-            const float z[3] = {s[0] + X[px * 3] + bias0, s[1] + X[px * 3 + 1] + bias1, s[2] + X[px * 3 + 2] + bias2};
+            if (col) {
+              const int yd = rr - 6;
+              const float* xs = X + a * 384 + px * 3;
+              const float z[3] = {s[0] + xs[0] + bias0, s[1] + xs[1] + bias1, s[2] + xs[2] + bias2};
 #pragma unroll
-            for (int co = 0; co < 3; co++) ob[(size_t)co * q.h * q.w + (size_t)yd * q.w] = 1.0f / (1.0f + expf(-z[co]));
+              for (int co = 0; co < 3; co++)
+                ob[(size_t)co * q.h * q.w + (size_t)yd * q.w] = 1.0f / (1.0f + expf(-z[co]));
+            }
             s[0] = s[1] = s[2] = 0.f;
           }
         }

@@ -7,7 +7,7 @@
 namespace lama {
 
 struct OutConvParams {
-  CUtensorMap amap;   // input: split bf16 (64, W + 6, H + 6, B, part), boxes of 64 x 128 x 1, 128B swizzle
+  CUtensorMap amap;   // input: split bf16 (64, W + 6, H + 6, B, part), boxes of 64 x 32 x 1, 128B swizzle
   CUtensorMap wmap;   // weights: split bf16 [2][160][64], n = ky * 21 + kx * 3 + co, boxes of 64 x 160
   const float* bias;  // [3]
   float* out;         // [B][3][H][W] fp32
