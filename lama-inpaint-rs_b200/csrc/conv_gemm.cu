@@ -51,8 +51,13 @@ __host__ __device__ constexpr uint32_t extra_smem(int bn) {
   return bn == 256 ? 8u * 32u * SHIFT_LD * 4u : tma_store_bn(bn) ? STAGING_OFF - 256u + 8u * STAGING_WARP : 0u;
 }
 __host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 2 * A_PART + 2u * (uint32_t)bn * 128u; }
+// TMEM accumulator buffers: four for tiles up to 128 columns wide, so the
+// epilogue (whose TMA stores share the TMA unit with the operand loads) may
+// fall up to three tiles behind the MMAs; two for wider tiles.
+__host__ __device__ constexpr int tmem_bufs_for(int bn) { return bn <= 128 ? 4 : 2; }
 __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
-  return 2 * bn <= 32 ? 32 : 2 * bn <= 64 ? 64 : 2 * bn <= 128 ? 128 : 2 * bn <= 256 ? 256 : 512;
+  const int c = tmem_bufs_for(bn) * bn;
+  return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512;
 }
 
 struct TileInfo {
@@ -371,14 +376,16 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
   constexpr uint32_t B_PART = (uint32_t)BROWS * 128u;
   constexpr uint32_t STAGE = stage_bytes(BROWS);
   constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  constexpr int NACC = tmem_bufs_for(BN);
   constexpr int CH = BN < 32 ? BN : 32;
   constexpr uint32_t IDESC = idesc_bf16_f32(BN, PAIR ? 256 : 128);
   static_assert(!(PAIR && SWAP), "CTA pairs use pixel-major tiles");
+  static_assert((2 * STAGES + 2 * NACC) * 8 + 12 <= 256, "barriers and TMEM slot fit the 256-byte block");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * NACC);
   // split-K verdict of the current tile (2 * tile sequence + last) and the
   // count of epilogue warps that have added their partial sums
   volatile int* split_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -388,7 +395,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
   auto tfull_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
-  auto tempty_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
+  auto tempty_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + NACC + a); };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -403,7 +410,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
     }
     *split_flag = -2;
     *split_cnt = 0;
-    for (int a = 0; a < 2; a++) {
+    for (int a = 0; a < NACC; a++) {
       mbar_init(tfull_bar(a), 1);
       mbar_init(tempty_bar(a), PAIR ? 16 : 256);  // pairs: one release per epilogue warp of both CTAs
     }
@@ -459,7 +466,6 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           const uint32_t sa = smem0 + (uint32_t)stage * STAGE;
           // activation sub-boxes: the A operand, or the B operand when swapped
           const uint32_t act = SWAP ? sa + 2 * A_PART : sa;
-          const uint32_t act_part = SWAP ? B_PART : A_PART;
           for (int u = 0; u < subs_per_kb; u++) {
             const int sub = kb * subs_per_kb + u;
             while (seg + 1 < C.nseg && sub >= C.seg[seg + 1].sub0) seg++;
@@ -469,25 +475,15 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
             const int cx = S.c0 + blk * p.cb;
             const int x = ti.j0 * S.stride + S.dx[tap];
             const int y = ti.i0 * S.stride + S.dy[tap];
-            if constexpr (PAIR) {
-              tma_load_5d_pair(act + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, fb);
-              tma_load_5d_pair(act + act_part + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 1, fb);
-            } else {
-              tma_load_5d(act + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, fb);
-              tma_load_5d(act + act_part + u * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 1, fb);
-            }
+            // one copy brings the hi and the lo sub-box (the map's boxes span both parts)
+            if constexpr (PAIR) tma_load_5d_pair(act + u * 2 * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, fb);
+            else tma_load_5d(act + u * 2 * sub_bytes, &p.amap[S.amap], cx, x, y, ti.b, 0, fb);
           }
           // weights: the B operand (BN rows), or the A operand (128 rows) when swapped
           const uint32_t wdst = SWAP ? sa : sa + 2 * A_PART;
-          const uint32_t wpart = SWAP ? A_PART : B_PART;
           const int wrow = SWAP ? ti.nt * 128 : ti.nt * BN + rank * BROWS;
-          if constexpr (PAIR) {
-            tma_load_3d_pair(wdst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
-            tma_load_3d_pair(wdst + wpart, &p.bmap[ti.cls], kb * 64, wrow, 1, fb);
-          } else {
-            tma_load_3d(wdst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
-            tma_load_3d(wdst + wpart, &p.bmap[ti.cls], kb * 64, wrow, 1, fb);
-          }
+          if constexpr (PAIR) tma_load_3d_pair(wdst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
+          else tma_load_3d(wdst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -504,8 +500,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       bool ok = true;
       for (int t = tfirst; t < p.total_tiles && ok; t += tstep, it++) {
         const TileInfo ti = decode_tile(p, t, rank);
-        const int acc = it & 1;
-        if (!mbar_wait(tempty_bar(acc), ((it >> 1) & 1) ^ 1, p.err, 2)) { ok = false; break; }
+        const int acc = it % NACC;
+        if (!mbar_wait(tempty_bar(acc), ((it / NACC) & 1) ^ 1, p.err, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = ti.kb0; kb < ti.kb1; kb++) {
@@ -515,9 +511,12 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           const uint32_t sb = sa + 2 * A_PART;
 #pragma unroll
           for (int k = 0; k < 4; k++) {
-            const uint32_t aoff = sw64 ? (uint32_t)((k >> 1) * 8192 + (k & 1) * 32) : (uint32_t)(k * 32);
+            // 64-byte swizzle (32-channel sub-boxes): [sub][part][128 px][32 ch];
+            // 128-byte swizzle: [part][128 px][64 ch]
+            const uint32_t aoff = sw64 ? (uint32_t)((k >> 1) * 16384 + (k & 1) * 32) : (uint32_t)(k * 32);
+            const uint32_t alo = sw64 ? 8192u : A_PART;
             const uint64_t a_hi = smem_desc(sa + aoff, a_sbo, a_layout);
-            const uint64_t a_lo = smem_desc(sa + A_PART + aoff, a_sbo, a_layout);
+            const uint64_t a_lo = smem_desc(sa + alo + aoff, a_sbo, a_layout);
             const uint64_t b_hi = smem_desc(sb + k * 32, 1024u, 2u);
             const uint64_t b_lo = smem_desc(sb + B_PART + k * 32, 1024u, 2u);
             if constexpr (PAIR) {
@@ -550,8 +549,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
     for (int t = tfirst; t < p.total_tiles; t += tstep, it++) {
       const TileInfo ti = decode_tile(p, t, rank);
       const GemmClass& C = p.cls[ti.cls];
-      const int acc = it & 1;
-      if (!mbar_wait(tfull_bar(acc), (it >> 1) & 1, p.err, 4)) break;
+      const int acc = it % NACC;
+      if (!mbar_wait(tfull_bar(acc), (it / NACC) & 1, p.err, 4)) break;
       tc_fence_after();
       const uint32_t trow = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
       if constexpr (SWAP) {

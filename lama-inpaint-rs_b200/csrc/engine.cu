@@ -122,7 +122,9 @@ struct Act {
   size_t bytes() const { return (size_t)part() * 2 * 2; }
 };
 
-CUtensorMap act_map(const Act& a, int cb, int bw, int bh, int stride, bool interior) {
+// Boxes of cb channels x (bw x bh) pixels; parts = 2 fetches the hi and lo
+// planes in one copy (the lo box lands right after the hi box).
+CUtensorMap act_map(const Act& a, int cb, int bw, int bh, int stride, bool interior, int parts = 1) {
   CUtensorMap m;
   const int hp = a.H + 2 * a.halo, wp = a.W + 2 * a.halo;
   char* base = (char*)a.p;
@@ -140,7 +142,7 @@ CUtensorMap act_map(const Act& a, int cb, int bw, int bh, int stride, bool inter
   dims[4] = 2;
   cuuint64_t strides[4] = {(cuuint64_t)a.C * 2, (cuuint64_t)wp * a.C * 2, (cuuint64_t)hp * wp * a.C * 2,
                            (cuuint64_t)a.part() * 2};
-  cuuint32_t box[5] = {(cuuint32_t)cb, (cuuint32_t)(bw * stride), (cuuint32_t)(bh * stride), 1, 1};
+  cuuint32_t box[5] = {(cuuint32_t)cb, (cuuint32_t)(bw * stride), (cuuint32_t)(bh * stride), 1, (cuuint32_t)parts};
   cuuint32_t estr[5] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1, 1};
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, base, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -223,11 +225,12 @@ struct GemmW {
   int nout = 0;
 };
 
-CUtensorMap w_map(const WClass& c, int bn) {
+// Boxes of 64 K x bn rows; parts = 2 as for act_map.
+CUtensorMap w_map(const WClass& c, int bn, int parts = 1) {
   CUtensorMap m;
   cuuint64_t dims[3] = {(cuuint64_t)c.k, (cuuint64_t)c.npad, 2};
   cuuint64_t strides[2] = {(cuuint64_t)c.k * 2, (cuuint64_t)c.npad * c.k * 2};
-  cuuint32_t box[3] = {64, (cuuint32_t)bn, 1};
+  cuuint32_t box[3] = {64, (cuuint32_t)bn, (cuuint32_t)parts};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c.w, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -678,7 +681,7 @@ struct Builder {
                       (e.tiling == LAMA_TILING_PAIRED || (e.tiling == LAMA_TILING_AUTO && p.m_tiles >= 2 * e.sms));
     p.pair = pair ? 1 : 0;
     for (size_t i = 0; i < amaps.size(); i++)
-      p.amap[i] = act_map(amaps[i].act, cb, bw, bh, amaps[i].stride, amaps[i].interior);
+      p.amap[i] = act_map(amaps[i].act, cb, bw, bh, amaps[i].stride, amaps[i].interior, 2);
     for (size_t i = amaps.size(); i < (size_t)GEMM_MAX_AMAPS; i++) p.amap[i] = p.amap[0];
     p.nclass = (int)classes.size();
     int tile0 = 0;
@@ -686,7 +689,7 @@ struct Builder {
       const ClassSpec& cs = classes[ci];
       GemmClass& C = p.cls[ci];
       const WClass& wc = Wt.cls[cs.wc];
-      p.bmap[ci] = w_map(wc, swap ? 128 : pair ? bn / 2 : bn);
+      p.bmap[ci] = w_map(wc, swap ? 128 : pair ? bn / 2 : bn, 2);
       C.n0 = cs.n0;
       C.nvalid = cs.nvalid;
       C.ntiles_n = swap ? cs.nvalid / 128 : (cs.nvalid + bn - 1) / bn;
