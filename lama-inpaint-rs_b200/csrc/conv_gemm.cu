@@ -447,7 +447,107 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
     }
   };
 
-  if (warp == 0) {
+  // Row-union stages: two normal stages each, A box (up to 6 rows x 32 pixels,
+  // both parts) at 0, the group's ndy B tiles (both parts each) from U_A.
+  constexpr uint32_t U_A = 6u * 32u * 128u * 2u;
+  constexpr int USTAGES = STAGES / 2;
+  static_assert(SWAP || BROWS != 64 || (STAGES % 2 == 0 && U_A + 3u * 2u * B_PART <= 2u * STAGE),
+                "row-union stages fit two normal stages");
+
+  if (warp == 0 && p.uni) {
+    // ---------------------------------------------------------- producer (row union)
+    if constexpr (!SWAP && BROWS == 64) {
+      if (lane == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = tfirst; t < p.total_tiles && ok; t += tstep) {
+          const TileInfo ti = decode_tile(p, t, rank);
+          const GemmClass& C = p.cls[ti.cls];
+          const int wrow = ti.nt * BN + rank * BROWS;
+          for (int g = 0; g < C.ngroup && ok; g++) {
+            const GemmGroup& G = C.grp[g];
+            const GemmSeg& S = C.seg[G.seg];
+            const uint32_t bytes = (uint32_t)p.urows[S.amap] * (uint32_t)p.bw * 256u + (uint32_t)G.ndy * 2u * B_PART;
+            for (int blk = 0; blk < S.nblk; blk++) {
+              if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, 1)) { ok = false; break; }
+              const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
+              if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), PAIR ? 2 * bytes : bytes);
+              const uint32_t sa = smem0 + (uint32_t)stage * 2u * STAGE;
+              const int cx = S.c0 + blk * 64, x = ti.j0 + G.dx, y = ti.i0 + G.dy0;
+              if constexpr (PAIR) tma_load_5d_pair(sa, &p.amap_u[S.amap], cx, x, y, ti.b, 0, fb);
+              else tma_load_5d(sa, &p.amap_u[S.amap], cx, x, y, ti.b, 0, fb);
+              for (int j = 0; j < G.ndy; j++) {
+                const int kb = S.sub0 + G.tap[j] * S.nblk + blk;
+                const uint32_t dst = sa + U_A + (uint32_t)j * 2u * B_PART;
+                if constexpr (PAIR) tma_load_3d_pair(dst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
+                else tma_load_3d(dst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
+              }
+              if (++stage == USTAGES) { stage = 0; phase ^= 1; }
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1 && p.uni) {
+    // ---------------------------------------------------------- MMA issuer (row union)
+    if constexpr (!SWAP && BROWS == 64) {
+      if (lane == 0 && rank == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        int it = 0;
+        bool ok = true;
+        for (int t = tfirst; t < p.total_tiles && ok; t += tstep, it++) {
+          const TileInfo ti = decode_tile(p, t, rank);
+          const GemmClass& C = p.cls[ti.cls];
+          const int acc = it % NACC;
+          if (!mbar_wait(tempty_bar(acc), ((it / NACC) & 1) ^ 1, p.err, 2)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+          uint32_t accum = 0;
+          for (int g = 0; g < C.ngroup && ok; g++) {
+            const GemmGroup& G = C.grp[g];
+            const GemmSeg& S = C.seg[G.seg];
+            const uint32_t rowb = (uint32_t)p.bw * 128u;                    // one pixel row of the box
+            const uint32_t apart = (uint32_t)p.urows[S.amap] * rowb;        // hi part of the box
+            for (int blk = 0; blk < S.nblk; blk++) {
+              if (!mbar_wait(full_bar(stage), phase, p.err, 3)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t sa = smem0 + (uint32_t)stage * 2u * STAGE;
+              for (int j = 0; j < G.ndy; j++) {
+                const uint32_t aj = sa + (uint32_t)j * rowb;
+                const uint32_t bj = sa + U_A + (uint32_t)j * 2u * B_PART;
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                  const uint64_t a_hi = smem_desc(aj + k * 32, 1024u, 2u);
+                  const uint64_t a_lo = smem_desc(aj + apart + k * 32, 1024u, 2u);
+                  const uint64_t b_hi = smem_desc(bj + k * 32, 1024u, 2u);
+                  const uint64_t b_lo = smem_desc(bj + B_PART + k * 32, 1024u, 2u);
+                  if constexpr (PAIR) {
+                    mma_bf16_pair(d_tmem, a_lo, b_hi, IDESC, accum);
+                    mma_bf16_pair(d_tmem, a_hi, b_lo, IDESC, 1u);
+                    mma_bf16_pair(d_tmem, a_hi, b_hi, IDESC, 1u);
+                  } else {
+                    mma_bf16(d_tmem, a_lo, b_hi, IDESC, accum);
+                    mma_bf16(d_tmem, a_hi, b_lo, IDESC, 1u);
+                    mma_bf16(d_tmem, a_hi, b_hi, IDESC, 1u);
+                  }
+                  accum = 1u;
+                }
+              }
+              if constexpr (PAIR) mma_commit_pair(empty_bar(stage), 3);
+              else mma_commit(empty_bar(stage));
+              if (++stage == USTAGES) { stage = 0; phase ^= 1; }
+            }
+          }
+          if (ok) {
+            if constexpr (PAIR) mma_commit_pair(tfull_bar(acc), 3);
+            else mma_commit(tfull_bar(acc));
+          }
+        }
+      }
+    }
+  } else if (warp == 0) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
       const int subs_per_kb = 64 / p.cb;

@@ -680,6 +680,50 @@ struct Builder {
     const bool pair = !swap && conv_gemm_pair_bn(bn) && e.pair_clusters > 0 &&
                       (e.tiling == LAMA_TILING_PAIRED || (e.tiling == LAMA_TILING_AUTO && p.m_tiles >= 2 * e.sms));
     p.pair = pair ? 1 : 0;
+    // Row union: 3x3-style taps that share dx read the row windows of one box
+    // of bh + 2 rows per 64-channel block instead of one box per tap.  Tiles
+    // of 4 x 32 pixels; the kernel's union stages exist for 64 B rows per CTA
+    // (BN = 64 single CTAs, BN = 128 pairs); split-K launches keep per-tap boxes.
+    std::vector<std::vector<GemmGroup>> groups(classes.size());
+    bool uni = !swap && cb == 64 && (pair ? bn == 128 : bn == 64) && mw % 32 == 0 && mh % 4 == 0;
+    bool multi = false;
+    for (size_t ci = 0; ci < classes.size() && uni; ci++) {
+      for (size_t si = 0; si < classes[ci].segs.size() && uni; si++) {
+        const SegSpec& ss = classes[ci].segs[si];
+        if (ss.stride != 1) { uni = false; break; }
+        std::vector<int> done(ss.taps.size(), 0);
+        for (size_t t0 = 0; t0 < ss.taps.size(); t0++) {
+          if (done[t0]) continue;
+          // the run of taps with this dx and dy = dy0, dy0 + 1, dy0 + 2
+          GemmGroup g{};
+          g.seg = (int8_t)si;
+          g.dx = (int8_t)ss.taps[t0].second;
+          g.dy0 = (int8_t)ss.taps[t0].first;
+          g.ndy = 0;
+          for (int d = 0; d < 3; d++) {
+            int found = -1;
+            for (size_t t = 0; t < ss.taps.size(); t++)
+              if (!done[t] && ss.taps[t].second == g.dx && ss.taps[t].first == g.dy0 + d) found = (int)t;
+            if (found < 0) break;
+            done[found] = 1;
+            g.tap[g.ndy++] = (int8_t)found;
+          }
+          multi = multi || g.ndy > 1;
+          groups[ci].push_back(g);
+        }
+      }
+      if (groups[ci].size() > (size_t)GEMM_MAX_GROUPS) uni = false;
+    }
+    uni = uni && multi;
+    if (uni) {
+      bh = 4;
+      bw = 32;
+      p.bh = bh;
+      p.bw = bw;
+      p.tiles_y = (mh + bh - 1) / bh;
+      p.tiles_x = (mw + bw - 1) / bw;
+      p.m_tiles = B * p.tiles_y * p.tiles_x;
+    }
     for (size_t i = 0; i < amaps.size(); i++)
       p.amap[i] = act_map(amaps[i].act, cb, bw, bh, amaps[i].stride, amaps[i].interior, 2);
     for (size_t i = amaps.size(); i < (size_t)GEMM_MAX_AMAPS; i++) p.amap[i] = p.amap[0];
@@ -732,6 +776,23 @@ struct Builder {
       if (C.ksplit > 1) ws_tiles += p.m_tiles * C.ntiles_n * C.ksplit;  // one slice per part
       C.tile0 = tile0;
       tile0 += (pair ? (p.m_tiles + 1) / 2 : p.m_tiles) * C.ntiles_n * C.ksplit;
+    }
+    if (uni && !ws_tiles) {
+      p.uni = 1;
+      int span[GEMM_MAX_AMAPS] = {1, 1, 1};
+      for (size_t ci = 0; ci < classes.size(); ci++) {
+        GemmClass& C = p.cls[ci];
+        C.ngroup = (int)groups[ci].size();
+        for (int g = 0; g < C.ngroup; g++) {
+          C.grp[g] = groups[ci][g];
+          const int a = C.seg[C.grp[g].seg].amap;
+          span[a] = std::max(span[a], (int)C.grp[g].ndy);
+        }
+      }
+      for (size_t i = 0; i < amaps.size(); i++) {
+        p.urows[i] = bh + span[i] - 1;
+        p.amap_u[i] = act_map(amaps[i].act, cb, bw, p.urows[i], 1, amaps[i].interior, 2);
+      }
     }
     if (ws_tiles) {
       p.ws = (float*)pl.mem.alloc((size_t)ws_tiles * bn * 128 * sizeof(float), false);

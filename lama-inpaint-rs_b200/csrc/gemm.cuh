@@ -28,6 +28,7 @@ constexpr int GEMM_MAX_TAPS = 49;
 constexpr int GEMM_MAX_SEGS = 2;
 constexpr int GEMM_MAX_CLASSES = 4;
 constexpr int GEMM_MAX_AMAPS = 3;
+constexpr int GEMM_MAX_GROUPS = 8;
 
 enum OutKind : int {
   OUT_SPLIT = 0,     // split bf16 NHWC (optionally halo'd, reflect-filled)
@@ -46,6 +47,15 @@ struct GemmSeg {
   int8_t dx[GEMM_MAX_TAPS];
 };
 
+// Row-union mode: taps of one segment that share dx and have consecutive dy
+// (up to 3) form a group; per 64-channel block the group's A tiles are the
+// row windows of ONE box of bh + ndy - 1 rows, loaded once.
+struct GemmGroup {
+  int8_t seg, dx, dy0, ndy;
+  int8_t tap[3];
+  int8_t pad;
+};
+
 struct GemmClass {
   int n0;        // first output channel (absolute, indexes scale/shift and out)
   int nvalid;    // output channels in this class
@@ -57,11 +67,19 @@ struct GemmClass {
   int ksplit;    // K parts per output tile (split-K; 1 = none)
   int ws_tile0;  // first workspace slice of the class (split-K)
   GemmSeg seg[GEMM_MAX_SEGS];
+  int ngroup;    // row-union mode: groups of the class's taps
+  GemmGroup grp[GEMM_MAX_GROUPS];
 };
 
 struct GemmParams {
   CUtensorMap amap[GEMM_MAX_AMAPS];
   CUtensorMap bmap[GEMM_MAX_CLASSES];
+  // row-union mode (uni = 1; tiles of bh = 4 x bw = 32 pixels, 64-channel
+  // boxes, stride 1, no split-K, BN = 64 or CTA pairs of BN = 128): per A map
+  // a map of boxes of urows = bh + (longest group) - 1 rows, both parts
+  CUtensorMap amap_u[GEMM_MAX_AMAPS];
+  int uni;
+  int urows[GEMM_MAX_AMAPS];
   // ostore != 0: the output leaves through TMA tensor stores of one box per
   // epilogue warp and 32-channel chunk (32 channels x obox_w x 32 / obox_w
   // pixels).  omap[c] views class c's output pixels (output = M pixel * mul +
