@@ -692,13 +692,15 @@ struct Builder {
         const SegSpec& ss = classes[ci].segs[si];
         if (ss.stride != 1) { uni = false; break; }
         std::vector<int> done(ss.taps.size(), 0);
-        for (size_t t0 = 0; t0 < ss.taps.size(); t0++) {
+        for (size_t t0 = 0; t0 < ss.taps.size(); t0 += done[t0] ? 1 : 0) {
           if (done[t0]) continue;
           // the run of taps with this dx and dy = dy0, dy0 + 1, dy0 + 2
           GemmGroup g{};
           g.seg = (int8_t)si;
           g.dx = (int8_t)ss.taps[t0].second;
           g.dy0 = (int8_t)ss.taps[t0].first;
+          for (size_t t = 0; t < ss.taps.size(); t++)  // start at the smallest dy left in this column
+            if (!done[t] && ss.taps[t].second == g.dx) g.dy0 = (int8_t)std::min<int>(g.dy0, ss.taps[t].first);
           g.ndy = 0;
           for (int d = 0; d < 3; d++) {
             int found = -1;
