@@ -275,9 +275,31 @@ __device__ __forceinline__ void store_split_tma(const GemmParams& p, const void*
   if (valid && p.out_halo && p.out_reflect) store_split_halo(p, b, oy, ox, n, hi, lo);
 }
 
+// Per-channel affine (folded BN / bias) and ReLU of CH channels starting at
+// class-relative channel nloc.  Whole chunks inside the class read the scale
+// and shift with 16-byte loads where both are 16-byte aligned (every lane
+// reads the same address, so each load is one broadcast).
 template <int CH>
 __device__ __forceinline__ void affine_relu(const GemmParams& p, const GemmClass& C, int nloc, float* v) {
   const int n = C.n0 + nloc;
+  if (CH % 4 == 0 && nloc + CH <= C.nvalid &&
+      ((reinterpret_cast<uintptr_t>(p.scale + n) | reinterpret_cast<uintptr_t>(p.shift + n)) & 15) == 0) {
+    const float4* s4 = reinterpret_cast<const float4*>(p.scale + n);
+    const float4* t4 = reinterpret_cast<const float4*>(p.shift + n);
+#pragma unroll
+    for (int q = 0; q < CH / 4; q++) {
+      const float4 s = __ldg(s4 + q), t = __ldg(t4 + q);
+      const float sv[4] = {s.x, s.y, s.z, s.w}, tv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        float x = v[4 * q + e] * sv[e];
+        x = x + tv[e];
+        if (p.relu) x = x > 0.f ? x : 0.f;
+        v[4 * q + e] = x;
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int k = 0; k < CH; k++) {
     int nn = n + k;
@@ -296,20 +318,7 @@ __device__ __forceinline__ void affine_relu(const GemmParams& p, const GemmClass
 template <int CH>
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const GemmClass& C, int b, int oy, int ox,
                                                int nloc, float* v) {
-  const int n = C.n0 + nloc;
-#pragma unroll
-  for (int k = 0; k < CH; k++) {
-    int nn = n + k;
-    float s = 1.f, t = 0.f;
-    if (nloc + k < C.nvalid) {
-      s = __ldg(p.scale + nn);
-      t = __ldg(p.shift + nn);
-    }
-    float x = v[k] * s;
-    x = x + t;
-    if (p.relu) x = x > 0.f ? x : 0.f;
-    v[k] = x;
-  }
+  affine_relu<CH>(p, C, nloc, v);
   store_channels<CH>(p, C, b, oy, ox, v, nloc);
 }
 
@@ -650,6 +659,27 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       const TileInfo ti = decode_tile(p, t, rank);
       const GemmClass& C = p.cls[ti.cls];
       const int acc = it % NACC;
+      if constexpr (!SWAP) {
+        // While the MMAs run: the scale / shift lines of this warp's chunks
+        // into L1 and the residual of its pixel into L2.
+        const int pi = ti.i0 + m / p.bw, pj = ti.j0 + m % p.bw;
+        const bool pv = pi < p.mh && pj < p.mw && !ti.dummy;
+        const int hp = p.out_h + 2 * p.out_halo, wp = p.out_w + 2 * p.out_halo;
+        const long long poff =
+            (((long long)ti.b * hp + pi * C.oy_mul + C.oy_add + p.out_halo) * wp + pj * C.ox_mul + C.ox_add +
+             p.out_halo) * p.out_c + C.n0;
+        for (int ch = half; ch < BN / 32; ch += 2) {
+          const int nloc = ti.nt * BN + ch * 32;
+          if (nloc >= C.nvalid) break;
+          if (lane == 0) prefetch_l1(p.scale + C.n0 + nloc);
+          if (lane == 1) prefetch_l1(p.shift + C.n0 + nloc);
+          if (p.skip && pv) {
+            const __nv_bfloat16* sb = reinterpret_cast<const __nv_bfloat16*>(p.skip) + poff + nloc;
+            prefetch_l2(sb);
+            prefetch_l2(sb + p.out_part);
+          }
+        }
+      }
       if (!mbar_wait(tfull_bar(acc), (it / NACC) & 1, p.err, 4)) break;
       tc_fence_after();
       const uint32_t trow = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
