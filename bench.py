@@ -261,8 +261,10 @@ def main():
 
     value = TOTAL_IMAGES * args.steps / (ms_dev / 1e3)
     e2e_value = TOTAL_IMAGES * args.steps / (ms_e2e / 1e3)
-    launches = eng.launch_count(chunks[0][1], SIZE, SIZE)  # kernels per chunk (same plan shape as u8 path + 2)
-    gpu_launches = (launches + 1) * len(chunks) * args.steps  # + composite; the f32 plan has no composite
+    # kernels per chunk: the u8 plan launches what the f32 plan does (its unfold
+    # reads u8, and the composite runs inside the OutConv kernel)
+    launches = eng.launch_count(chunks[0][1], SIZE, SIZE)
+    gpu_launches = launches * len(chunks) * args.steps
 
     result = None
     if rank == 0:

@@ -476,7 +476,7 @@ void load_weights(const WeightFile& wf, Weights& W) {
 }
 
 // ------------------------------------------------------------------ ops
-enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_IRFFT_PAR, OP_OUTCONV, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_COMPOSITE, OP_TO_SPLIT, OP_TO_NCHW };
+enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_IRFFT_PAR, OP_OUTCONV, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_TO_SPLIT, OP_TO_NCHW };
 
 struct Op {
   OpKind kind;
@@ -487,7 +487,6 @@ struct Op {
   std::unique_ptr<OutConvParams> oc;
   FftParams f{};
   UnfoldParams u{};
-  CompositeParams c{};
   ConvertParams cv{};
   double flops = 0, bytes = 0;
   // output tensor, for the diagnostics entry points: split bf16 or fp32,
@@ -511,7 +510,6 @@ int launch_op(const Op& op, cudaStream_t st) {
     case OP_OUTCONV: return launch_outconv(*op.oc, op.grid, st);
     case OP_UNFOLD_F32: return launch_unfold_f32(op.u, st);
     case OP_UNFOLD_U8: return launch_unfold_u8(op.u, st);
-    case OP_COMPOSITE: return launch_composite(op.c, st);
     case OP_TO_SPLIT: return launch_nchw_to_split(op.cv, st);
     case OP_TO_NCHW: return launch_split_to_nchw(op.cv, st);
   }
@@ -968,7 +966,8 @@ struct Builder {
       }
   }
 
-  void core(const Act& U, int B, int H, int W, float* out) {
+  // comp: the u8 path's composite, fused into the OutConv (out is then unused)
+  void core(const Act& U, int B, int H, int W, float* out, const CompositeParams* comp = nullptr) {
     const int h2 = H / 2, w2 = W / 2, h4 = H / 4, w4 = W / 4, h8 = H / 8, w8 = W / 8;
     Act X1 = act(B, H, W, 64, 1);
     Act X2 = act(B, h2, w2, 128, 1);
@@ -1041,6 +1040,13 @@ struct Builder {
       q.wmap = w_map(e.W.outc.cls[0], 160);
       q.bias = e.W.outc.shift;
       q.out = out;
+      if (comp) {
+        q.rgb = comp->rgb;
+        q.mask = comp->mask;
+        q.dst = comp->dst;
+        q.ih = comp->h;
+        q.iw = comp->w;
+      }
       q.batch = B;
       q.h = H;
       q.w = W;
@@ -1073,7 +1079,7 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
   Builder b{*e, *pl};
   if (kind == 0 || kind == 1) {
     Act U = b.act(B, H + 6, W, 32, 0);
-    pl->out = (float*)pl->mem.alloc((size_t)B * 3 * H * W * 4);
+    if (kind == 0) pl->out = (float*)pl->mem.alloc((size_t)B * 3 * H * W * 4);
     Op un;
     un.name = "unfold_input";
     un.u.batch = B; un.u.H = H; un.u.W = W; un.u.h = h; un.u.w = w;
@@ -1094,13 +1100,11 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
       un.u.mask = pl->mask;
     }
     pl->ops.push_back(std::move(un));
-    b.core(U, B, H, W, pl->out);
     if (kind == 1) {
-      Op c;
-      c.kind = OP_COMPOSITE;
-      c.name = "composite";
-      c.c = CompositeParams{B, h, w, H, W, pl->rgb, pl->mask, pl->out, pl->out_rgb};
-      pl->ops.push_back(std::move(c));
+      const CompositeParams comp{B, h, w, H, W, pl->rgb, pl->mask, nullptr, pl->out_rgb};
+      b.core(U, B, H, W, nullptr, &comp);
+    } else {
+      b.core(U, B, H, W, pl->out);
     }
   } else {
     Act XA = b.act(B, H, W, 512, 1);

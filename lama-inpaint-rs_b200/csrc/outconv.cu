@@ -245,9 +245,29 @@ __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__
               const int yd = rr - 6;
               const float* xs = X + a * 384 + px * 3;
               const float z[3] = {s[0] + xs[0] + bias0, s[1] + xs[1] + bias1, s[2] + xs[2] + bias2};
+              if (q.dst) {
+                const int y = y0 + yd, x = x0 + ox;
+                if (y < q.ih && x < q.iw) {
+                  const size_t pix = ((size_t)b * q.ih + y) * q.iw + x;
+                  uint8_t* d = q.dst + pix * 3;
+                  if (q.mask[pix] == 0) {
+                    const uint8_t* r = q.rgb + pix * 3;
+                    d[0] = r[0];
+                    d[1] = r[1];
+                    d[2] = r[2];
+                  } else {
 #pragma unroll
-              for (int co = 0; co < 3; co++)
-                ob[(size_t)co * q.h * q.w + (size_t)yd * q.w] = 1.0f / (1.0f + expf(-z[co]));
+                    for (int co = 0; co < 3; co++) {
+                      const float v = fminf(fmaxf(1.0f / (1.0f + expf(-z[co])), 0.0f), 1.0f) * 255.0f;
+                      d[co] = (uint8_t)(int)(v + 0.5f);
+                    }
+                  }
+                }
+              } else {
+#pragma unroll
+                for (int co = 0; co < 3; co++)
+                  ob[(size_t)co * q.h * q.w + (size_t)yd * q.w] = 1.0f / (1.0f + expf(-z[co]));
+              }
             }
             s[0] = s[1] = s[2] = 0.f;
           }

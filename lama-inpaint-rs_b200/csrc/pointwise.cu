@@ -8,7 +8,8 @@
 //               The output U[b][y][x][kx*4 + c] (32 channels, 28 used) is the
 //               A operand of model.1: seven taps along x packed into channels,
 //               so the 7x7 conv becomes 8 row-taps of 32 channels.
-// k_composite : the mask composite + u8 quantisation (lama-rs/src/main.rs:272-307).
+// (The mask composite + u8 quantisation, lama-rs/src/main.rs:272-307, runs in
+// the OutConv epilogue, outconv.cu.)
 // k_nchw_to_split / k_split_to_nchw : the resblock-stack entry point's layout
 //               conversions (fp32 NCHW <-> split-bf16 NHWC with reflect halo).
 #include <cstdint>
@@ -86,32 +87,6 @@ __global__ void k_unfold(UnfoldParams p) {
   }
 }
 
-__global__ void k_composite(CompositeParams p) {
-  const long long total = (long long)p.batch * p.h * p.w;
-  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= total) return;
-  const int x = (int)(idx % p.w);
-  const long long t = idx / p.w;
-  const int y = (int)(t % p.h);
-  const int b = (int)(t / p.h);
-  const uint8_t* src = p.rgb + (size_t)idx * 3;
-  uint8_t* dst = p.dst + (size_t)idx * 3;
-  if (p.mask[idx] == 0) {
-    dst[0] = src[0];
-    dst[1] = src[1];
-    dst[2] = src[2];
-    return;
-  }
-  const size_t plane = (size_t)p.H * p.W;
-  const float* o = p.net + (size_t)b * 3 * plane + (size_t)y * p.W + x;
-#pragma unroll
-  for (int c = 0; c < 3; c++) {
-    float v = o[c * plane];
-    v = fminf(fmaxf(v, 0.0f), 1.0f) * 255.0f;
-    dst[c] = (uint8_t)(int)(v + 0.5f);
-  }
-}
-
 // fp32 NCHW [B][C][h][w] -> channels [c0, c0+C) of split NHWC [2][B][h+2halo][w+2halo][Ct], reflect halo
 __global__ void k_nchw_to_split(ConvertParams p) {
   const long long total = (long long)p.batch * (p.h + 2 * p.halo) * (p.w + 2 * p.halo) * p.c;
@@ -162,12 +137,6 @@ int launch_unfold_f32(const UnfoldParams& p, cudaStream_t st) {
 int launch_unfold_u8(const UnfoldParams& p, cudaStream_t st) {
   const long long n = (long long)p.batch * (p.H + 6) * p.W;
   k_unfold<true><<<blocks_for(n, 128), 128, 0, st>>>(p);
-  return (int)cudaGetLastError();
-}
-
-int launch_composite(const CompositeParams& p, cudaStream_t st) {
-  const long long n = (long long)p.batch * p.h * p.w;
-  k_composite<<<blocks_for(n, 256), 256, 0, st>>>(p);
   return (int)cudaGetLastError();
 }
 

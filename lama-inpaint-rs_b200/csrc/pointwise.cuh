@@ -17,11 +17,12 @@ struct UnfoldParams {
   long long out_part;
 };
 
+// The u8 path's composite (fused into the OutConv, outconv.cu).
 struct CompositeParams {
   int batch, h, w, H, W;
   const uint8_t* rgb;      // [B][h][w][3]
   const uint8_t* mask;     // [B][h][w]
-  const float* net;        // [B][3][H][W] sigmoid output
+  const float* net;        // [B][3][H][W] sigmoid output (unused by the fused composite)
   uint8_t* dst;            // [B][h][w][3]
 };
 
@@ -34,7 +35,6 @@ struct ConvertParams {
 
 int launch_unfold_f32(const UnfoldParams& p, cudaStream_t st);
 int launch_unfold_u8(const UnfoldParams& p, cudaStream_t st);
-int launch_composite(const CompositeParams& p, cudaStream_t st);
 int launch_nchw_to_split(const ConvertParams& p, cudaStream_t st);
 int launch_split_to_nchw(const ConvertParams& p, cudaStream_t st);
 
