@@ -161,6 +161,18 @@ int lama_debug_read(lama_engine* e, int batch, int h, int w, int op, float* out,
  * no GPU fault or hang is involved.  limit_ms in 1..1000. */
 int lama_debug_wait_timeout(lama_engine* e, int limit_ms);
 
+/* --sections on the device (lama-rs/src/main.rs:465-566, the per-pass crop,
+ * inference, composite and paste of the reference's loop): the w x h image
+ * and mask go up once, then for each of the n rectangles rects[4i..4i+3] =
+ * {x0, y0, x1, y1} (from lama_section_rects, rim first) one pass runs on the
+ * side x side window centred on it (lama_window_origin), with the mask
+ * restricted to the rectangle, and its fill is written into the
+ * device-resident working image, which the next pass reads; the result comes
+ * back once.  side = min(512, w, h) as in the reference.  n = 0 copies rgb.
+ * Returns LAMA_EINVAL for a rectangle outside the image or its window. */
+int lama_inpaint_sections_u8(lama_engine* e, const uint8_t* rgb, const uint8_t* mask, int w, int h,
+                             const int* rects, int n, int side, uint8_t* out_rgb);
+
 /* Host helpers of the CLI's --tile / --sections modes (no GPU needed).
  * They restate lama-rs/src/main.rs's geometry with the same constants
  * (window >= 512, sections of 256, multiples of 8) and ordering. */

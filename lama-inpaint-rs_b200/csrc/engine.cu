@@ -564,12 +564,13 @@ void choose_tile(int mh, int mw, int& bh, int& bw, int px = 128, int stride = 1)
 
 // ------------------------------------------------------------------ engine
 struct Plan {
-  int kind = 0;  // 0 f32 forward, 1 u8 inpaint, 2 resblocks
+  int kind = 0;  // 0 f32 forward, 1 u8 inpaint, 2 resblocks, 3 one --sections pass (window)
   int B = 0, H = 0, W = 0, h = 0, w = 0, nblocks = 0;
   DevMem mem;
   float* in_f32 = nullptr;
   float* out = nullptr;
   uint8_t *rgb = nullptr, *mask = nullptr, *out_rgb = nullptr;
+  WinDesc* win = nullptr;  // kind 3: the pass's window, read by the kernels at run time
   float *l_in = nullptr, *g_in = nullptr, *l_out = nullptr, *g_out = nullptr;
   std::vector<Op> ops;
   cudaGraphExec_t exec = nullptr;
@@ -590,6 +591,12 @@ struct lama_engine {
   int spectral = LAMA_SPECTRAL_AUTO;
   int pair_clusters = 0;  // co-resident CTA-pair clusters (0: no pair tiles)
   std::map<std::tuple<int, int, int, int, int, int, int>, std::unique_ptr<Plan>> plans;
+  // --sections: the device-resident working image, mask and pass windows
+  DevMem sec_mem;
+  uint8_t* sec_img = nullptr;
+  uint8_t* sec_mask = nullptr;
+  WinDesc* sec_desc = nullptr;
+  size_t sec_px = 0, sec_n = 0;
 };
 
 namespace {
@@ -967,7 +974,9 @@ struct Builder {
   }
 
   // comp: the u8 path's composite, fused into the OutConv (out is then unused)
-  void core(const Act& U, int B, int H, int W, float* out, const CompositeParams* comp = nullptr) {
+  // win: one --sections pass, fill written into the working image (out unused)
+  void core(const Act& U, int B, int H, int W, float* out, const CompositeParams* comp = nullptr,
+            const WinDesc* win = nullptr) {
     const int h2 = H / 2, w2 = W / 2, h4 = H / 4, w4 = W / 4, h8 = H / 8, w8 = W / 8;
     Act X1 = act(B, H, W, 64, 1);
     Act X2 = act(B, h2, w2, 128, 1);
@@ -1040,6 +1049,7 @@ struct Builder {
       q.wmap = w_map(e.W.outc.cls[0], 160);
       q.bias = e.W.outc.shift;
       q.out = out;
+      q.win = win;
       if (comp) {
         q.rgb = comp->rgb;
         q.mask = comp->mask;
@@ -1077,7 +1087,7 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
   std::unique_ptr<Plan> pl(new Plan());
   pl->kind = kind; pl->B = B; pl->H = H; pl->W = W; pl->h = h; pl->w = w; pl->nblocks = nblocks;
   Builder b{*e, *pl};
-  if (kind == 0 || kind == 1) {
+  if (kind == 0 || kind == 1 || kind == 3) {
     Act U = b.act(B, H + 6, W, 32, 0);
     if (kind == 0) pl->out = (float*)pl->mem.alloc((size_t)B * 3 * H * W * 4);
     Op un;
@@ -1091,6 +1101,10 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
       pl->in_f32 = (float*)pl->mem.alloc((size_t)B * 4 * H * W * 4);
       un.kind = OP_UNFOLD_F32;
       un.u.in = pl->in_f32;
+    } else if (kind == 3) {
+      pl->win = (WinDesc*)pl->mem.alloc(sizeof(WinDesc));
+      un.kind = OP_UNFOLD_U8;
+      un.u.win = pl->win;
     } else {
       pl->rgb = (uint8_t*)pl->mem.alloc((size_t)B * h * w * 3);
       pl->mask = (uint8_t*)pl->mem.alloc((size_t)B * h * w);
@@ -1103,6 +1117,9 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
     if (kind == 1) {
       const CompositeParams comp{B, h, w, H, W, pl->rgb, pl->mask, nullptr, pl->out_rgb};
       b.core(U, B, H, W, nullptr, &comp);
+    } else if (kind == 3) {
+      const CompositeParams comp{B, h, w, H, W, nullptr, nullptr, nullptr, nullptr};
+      b.core(U, B, H, W, nullptr, &comp, pl->win);
     } else {
       b.core(U, B, H, W, pl->out);
     }
@@ -1297,6 +1314,57 @@ int lama_inpaint_u8_device(lama_engine* e, const uint8_t* d_rgb, const uint8_t* 
   });
 }
 
+int lama_inpaint_sections_u8(lama_engine* e, const uint8_t* rgb, const uint8_t* mask, int w, int h, const int* rects,
+                             int n, int side, uint8_t* out_rgb) {
+  return guarded(e, [&] {
+    if (!rgb || !mask || !out_rgb || (n > 0 && !rects)) throw EngineError{LAMA_EINVAL, "null buffer"};
+    if (w < 1 || h < 1 || n < 0) throw EngineError{LAMA_EINVAL, "w, h must be positive and n non-negative"};
+    const size_t npx = (size_t)w * h;
+    if (n == 0) {
+      memcpy(out_rgb, rgb, npx * 3);
+      return;
+    }
+    if (side < 1 || side > std::min(w, h)) throw EngineError{LAMA_EINVAL, "side must be in 1..min(w, h)"};
+    std::vector<WinDesc> d((size_t)n);
+    for (int i = 0; i < n; i++) {
+      const int* r = rects + 4 * i;
+      if (r[0] < 0 || r[1] < 0 || r[2] > w || r[3] > h || r[0] >= r[2] || r[1] >= r[3])
+        throw EngineError{LAMA_EINVAL, "section " + std::to_string(i) + " is not a non-empty rectangle inside the image"};
+      const int wx0 = lama_window_origin((r[0] + r[2]) / 2, side, w), wy0 = lama_window_origin((r[1] + r[3]) / 2, side, h);
+      if (r[0] < wx0 || r[1] < wy0 || r[2] > wx0 + side || r[3] > wy0 + side)
+        throw EngineError{LAMA_EINVAL, "section " + std::to_string(i) + " does not fit its window"};
+      d[i] = WinDesc{nullptr, nullptr, w, h, wx0, wy0, r[0], r[1], r[2], r[3]};
+    }
+    const int S = (side + 7) / 8 * 8;
+    check_shape(1, side, side, false);
+    Plan& pl = get_plan(e, 3, 1, S, S, side, side, 18);
+    if (e->sec_px < npx || e->sec_n < (size_t)n) {  // grow the device-resident buffers
+      sync_check(e);
+      e->sec_mem.free_all();
+      e->sec_px = std::max(e->sec_px, npx);
+      e->sec_n = std::max(e->sec_n, (size_t)n);
+      e->sec_img = (uint8_t*)e->sec_mem.alloc(e->sec_px * 3, false);
+      e->sec_mask = (uint8_t*)e->sec_mem.alloc(e->sec_px, false);
+      e->sec_desc = (WinDesc*)e->sec_mem.alloc(e->sec_n * sizeof(WinDesc), false);
+    }
+    for (auto& x : d) {
+      x.img = e->sec_img;
+      x.mask = e->sec_mask;
+    }
+    CK(cudaMemcpyAsync(e->sec_img, rgb, npx * 3, cudaMemcpyHostToDevice, e->stream));
+    CK(cudaMemcpyAsync(e->sec_mask, mask, npx, cudaMemcpyHostToDevice, e->stream));
+    CK(cudaMemcpyAsync(e->sec_desc, d.data(), (size_t)n * sizeof(WinDesc), cudaMemcpyHostToDevice, e->stream));
+    // pass i reads its window of the working image, which holds the fills of
+    // passes 0..i-1, and writes its own fill back (stream order)
+    for (int i = 0; i < n; i++) {
+      CK(cudaMemcpyAsync(pl.win, e->sec_desc + i, sizeof(WinDesc), cudaMemcpyDeviceToDevice, e->stream));
+      run_plan(e, pl);
+    }
+    CK(cudaMemcpyAsync(out_rgb, e->sec_img, npx * 3, cudaMemcpyDeviceToHost, e->stream));
+    sync_check(e);
+  });
+}
+
 static int resblocks_impl(lama_engine* e, const float* l_in, const float* g_in, int batch, int h, int w, int nblocks,
                           float* l_out, float* g_out, cudaMemcpyKind kin, cudaMemcpyKind kout, bool sync) {
   return guarded(e, [&] {
@@ -1476,6 +1544,7 @@ void lama_close(lama_engine* e) {
     cudaStreamSynchronize(e->stream);
   }
   e->plans.clear();
+  e->sec_mem.free_all();
   e->wmem.free_all();
   if (e->stream) cudaStreamDestroy(e->stream);
   cudaGetLastError();

@@ -245,7 +245,20 @@ __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__
               const int yd = rr - 6;
               const float* xs = X + a * 384 + px * 3;
               const float z[3] = {s[0] + xs[0] + bias0, s[1] + xs[1] + bias1, s[2] + xs[2] + bias2};
-              if (q.dst) {
+              if (q.win) {
+                const int y = y0 + yd, x = x0 + ox;
+                const WinDesc& d = *q.win;
+                const int gy = d.wy0 + y, gx = d.wx0 + x;
+                if (y < q.ih && x < q.iw && gx >= d.sx0 && gx < d.sx1 && gy >= d.sy0 && gy < d.sy1 &&
+                    d.mask[(size_t)gy * d.fw + gx] != 0) {
+                  uint8_t* o = d.img + ((size_t)gy * d.fw + gx) * 3;
+#pragma unroll
+                  for (int co = 0; co < 3; co++) {
+                    const float v = fminf(fmaxf(1.0f / (1.0f + expf(-z[co])), 0.0f), 1.0f) * 255.0f;
+                    o[co] = (uint8_t)(int)(v + 0.5f);
+                  }
+                }
+              } else if (q.dst) {
                 const int y = y0 + yd, x = x0 + ox;
                 if (y < q.ih && x < q.iw) {
                   const size_t pix = ((size_t)b * q.ih + y) * q.iw + x;

@@ -6,6 +6,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "pointwise.cuh"
+
 namespace lama {
 
 struct OutConvParams {
@@ -21,6 +23,9 @@ struct OutConvParams {
   const uint8_t* mask;
   uint8_t* dst;
   int ih, iw;
+  // window mode (one --sections pass, batch 1): write the fill into win->img
+  // at the window's place, where the mask is set inside the section rectangle
+  const WinDesc* win;
   int batch, h, w;
   int strips, segs, seg;  // filled by outconv_units (seg = output rows per segment)
   int* err;           // device status word

@@ -62,6 +62,19 @@ __global__ void k_unfold(UnfoldParams p) {
   for (int kx = 0; kx < 7; kx++) {
     const int xx = reflect_i(x + kx - 3, p.W);
     if constexpr (U8) {
+      if (p.win) {
+        // window pixel (reflect-extended inside the side x side window) of the working image
+        const WinDesc& d = *p.win;
+        const int gy = d.wy0 + reflect_i(yy, p.h), gx = d.wx0 + reflect_i(xx, p.w);
+        const bool in = gx >= d.sx0 && gx < d.sx1 && gy >= d.sy0 && gy < d.sy1;
+        const float m = in && d.mask[(size_t)gy * d.fw + gx] != 0 ? 1.0f : 0.0f;
+        const uint8_t* px = d.img + ((size_t)gy * d.fw + gx) * 3;
+        const float om = 1.0f - m;
+#pragma unroll
+        for (int c = 0; c < 3; c++) v[4 * kx + c] = ((float)px[c] / 255.0f) * om;
+        v[4 * kx + 3] = m;
+        continue;
+      }
       const uint8_t* rgb = p.rgb + (size_t)b * p.h * p.w * 3;
       const uint8_t* mask = p.mask + (size_t)b * p.h * p.w;
       input_px_u8(rgb, mask, p.h, p.w, yy, xx, v + 4 * kx);

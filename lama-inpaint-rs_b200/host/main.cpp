@@ -240,32 +240,25 @@ int run(const Args& a) {
       const int side = std::max(1, std::min(kTileMin, std::min(W, H)));
       snprintf(msg, sizeof(msg), "sections: %d passes, %dx%d window each, rim inward", n, side, side);
       log(msg);
-      out = src;  // the working image: original plus the fills of earlier passes
       for (int i = 0; i < n; i++) {
         const int sx0 = rects[4 * i], sy0 = rects[4 * i + 1], sx1 = rects[4 * i + 2], sy1 = rects[4 * i + 3];
-        const int wx0 = lama_window_origin((sx0 + sx1) / 2, side, W);
-        const int wy0 = lama_window_origin((sy0 + sy1) / 2, side, H);
-        Rgb8 sub = crop_rgb(out, wx0, wy0, side);
-        std::vector<uint8_t> sub_mask = crop_gray(mask, W, wx0, wy0, side);
-        for (int y = 0; y < side; y++)
-          for (int x = 0; x < side; x++) {
-            const int gx = wx0 + x, gy = wy0 + y;
-            if (!(gx >= sx0 && gx < sx1 && gy >= sy0 && gy < sy1)) sub_mask[(size_t)y * side + x] = 0;
-          }
-        const auto t0 = std::chrono::steady_clock::now();
-        Rgb8 filled;
-        if (!inpaint(eng, sub, sub_mask, filled, err)) { log("error: " + err); return 1; }
-        snprintf(msg, sizeof(msg), "  pass %d/%d: %dx%d window at (%d,%d), %.2fs", i + 1, n, side, side, wx0, wy0,
-                 secs(t0));
+        snprintf(msg, sizeof(msg), "  pass %d/%d: %dx%d window at (%d,%d)", i + 1, n, side, side,
+                 lama_window_origin((sx0 + sx1) / 2, side, W), lama_window_origin((sy0 + sy1) / 2, side, H));
         log(msg);
-        for (int gy = sy0; gy < sy1; gy++)
-          for (int gx = sx0; gx < sx1; gx++) {
-            if (!mask[(size_t)gy * W + gx]) continue;
-            const size_t o = ((size_t)gy * W + gx) * 3;
-            const size_t so = ((size_t)(gy - wy0) * side + (gx - wx0)) * 3;
-            memcpy(&out.data[o], &filled.data[so], 3);
-          }
       }
+      // every pass on the GPU: the working image (original plus the fills of
+      // earlier passes) stays on the device between passes
+      const auto t0 = std::chrono::steady_clock::now();
+      out.width = W;
+      out.height = H;
+      out.data.resize(src.data.size());
+      if (lama_inpaint_sections_u8(eng.e, src.data.data(), mask.data(), W, H, rects.data(), n, side,
+                                   out.data.data()) != 0) {
+        log(std::string("error: gpu inference failed: ") + lama_last_error(eng.e));
+        return 1;
+      }
+      snprintf(msg, sizeof(msg), "inference: %d passes in %.2fs", n, secs(t0));
+      log(msg);
     }
   } else if (a.tile) {
     // main.rs:378-443

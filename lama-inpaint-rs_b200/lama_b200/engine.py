@@ -53,6 +53,8 @@ SIGNATURES = [
     ("lama_forward_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("lama_inpaint_u8", ctypes.c_int, [_vp, _u8p, _u8p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _u8p]),
     ("lama_inpaint_u8_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    ("lama_inpaint_sections_u8", ctypes.c_int, [_vp, _u8p, _u8p, ctypes.c_int, ctypes.c_int,
+                                                ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int, _u8p]),
     ("lama_resblocks", ctypes.c_int, [_vp, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       _f32p, _f32p]),
     ("lama_resblocks_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -221,6 +223,21 @@ class Engine:
         out = np.empty_like(rgb)
         self._check(lib().lama_inpaint_u8(self._h, _up(rgb), _up(mask), b, h, w, _up(out)))
         return out[0] if single else out
+
+    def inpaint_sections_u8(self, rgb: np.ndarray, mask: np.ndarray, rects, side: int) -> np.ndarray:
+        """--sections on the device: rgb [h,w,3] u8, mask [h,w] u8, rects [(x0, y0, x1, y1), ...]
+        (lama_section_rects order), one side x side window per rectangle."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        mask = np.ascontiguousarray(mask, np.uint8)
+        h, w, _ = rgb.shape
+        if mask.shape != (h, w):
+            raise LamaError(-1, f"mask is {mask.shape[-1]}x{mask.shape[-2]} but image is {w}x{h}")
+        r = np.ascontiguousarray(np.asarray(rects, np.int32).reshape(-1, 4))
+        out = np.empty_like(rgb)
+        self._check(lib().lama_inpaint_sections_u8(self._h, _up(rgb), _up(mask), w, h,
+                                                   r.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), len(r), side,
+                                                   _up(out)))
+        return out
 
     def inpaint_u8_device(self, d_rgb: int, d_mask: int, d_out: int, batch: int, h: int, w: int):
         self._check(lib().lama_inpaint_u8_device(self._h, d_rgb, d_mask, batch, h, w, d_out))

@@ -85,6 +85,49 @@ def test_cli_sections_follow_the_reference_orchestration(tmp_path, weights_tamed
     np.testing.assert_array_equal(got, working)
 
 
+def _host_sections(engine, img, m):
+    """The reference's --sections loop (main.rs:465-566) written on the host:
+    crop the working image, restrict the mask to the section, inpaint, paste."""
+    h, w = m.shape
+    working = img.copy()
+    side = min(512, w, h)
+    for x0, y0, x1, y1 in section_rects(m):
+        wx = window_origin((x0 + x1) // 2, side, w)
+        wy = window_origin((y0 + y1) // 2, side, h)
+        sub = working[wy:wy + side, wx:wx + side].copy()
+        sm = m[wy:wy + side, wx:wx + side].copy()
+        yy, xx = np.mgrid[wy:wy + side, wx:wx + side]
+        sm[~((xx >= x0) & (xx < x1) & (yy >= y0) & (yy < y1))] = 0
+        filled = engine.inpaint_u8(sub, sm)
+        blk = m[y0:y1, x0:x1] > 0
+        working[y0:y1, x0:x1][blk] = filled[y0 - wy:y1 - wy, x0 - wx:x1 - wx][blk]
+    return working
+
+
+@pytest.mark.parametrize("h,w,kind,seed", [(700, 760, "rect", 61), (530, 610, "brush", 62), (300, 420, "rect", 63)])
+def test_device_sections_match_the_host_loop(engine_tamed, h, w, kind, seed):
+    """lama_inpaint_sections_u8 keeps the working image on the GPU between
+    passes; it must give the host loop's bytes exactly."""
+    img = seeded.value_noise(h, w, seed)
+    if kind == "rect":
+        m = seeded.rect_mask(h, w, w // 7, h // 6, w // 2 + 40, h // 2 + 30)  # x0, y0, width, height
+    else:
+        m = np.maximum(seeded.brush_mask(h, w, seed), seeded.rect_mask(h, w, 40, 50, w - 100, h - 90))
+    rects = section_rects(m)
+    side = min(512, w, h)
+    got = engine_tamed.inpaint_sections_u8(img, m, rects, side)
+    np.testing.assert_array_equal(got, _host_sections(engine_tamed, img, m))
+    np.testing.assert_array_equal(got[m == 0], img[m == 0])
+
+
+def test_device_sections_reject_a_rectangle_outside_its_window(engine_tamed):
+    img = seeded.value_noise(600, 600, 64)
+    m = seeded.rect_mask(600, 600, 10, 10, 580, 580)
+    with pytest.raises(Exception, match="EINVAL"):
+        engine_tamed.inpaint_sections_u8(img, m, [(0, 0, 600, 600)], 512)
+    np.testing.assert_array_equal(engine_tamed.inpaint_sections_u8(img, m, [], 512), img)
+
+
 def test_cli_stdin_and_stdout(tmp_path, weights_tamed, engine_tamed):
     img = seeded.value_noise(48, 56, 54)
     m = seeded.brush_mask(48, 56, 54)
