@@ -23,6 +23,7 @@
 // TMEM holds two BN-column accumulators so the epilogue of one tile overlaps
 // the main loop of the next.
 #include <algorithm>
+#include <type_traits>
 #include <cstdio>
 
 #include "gemm.cuh"
@@ -456,8 +457,10 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
     }
   };
 
-  // Row-union stages: two normal stages each, A box (up to 6 rows x 32 pixels,
-  // both parts) at 0, the group's ndy B tiles (both parts each) from U_A.
+  // Row-union stages: two normal stages each, A box (up to 6 rows x 32 pixels
+  // of 64 channels, or 7 rows of 32 channels; both parts) at 0, the group's
+  // weight K blocks (both parts each) from U_A.  With 32-channel boxes a K
+  // block holds two taps (tap parity = which half of its 128-byte row).
   constexpr uint32_t U_A = 6u * 32u * 128u * 2u;
   constexpr int USTAGES = STAGES / 2;
   static_assert(SWAP || BROWS != 64 || (STAGES % 2 == 0 && U_A + 3u * 2u * B_PART <= 2u * STAGE),
@@ -477,17 +480,19 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           for (int g = 0; g < C.ngroup && ok; g++) {
             const GemmGroup& G = C.grp[g];
             const GemmSeg& S = C.seg[G.seg];
-            const uint32_t bytes = (uint32_t)p.urows[S.amap] * (uint32_t)p.bw * 256u + (uint32_t)G.ndy * 2u * B_PART;
+            const int tsh = p.cb == 32 ? 1 : 0;                          // log2(taps per K block)
+            const uint32_t bytes = (uint32_t)p.urows[S.amap] * (uint32_t)p.bw * (uint32_t)p.cb * 4u +
+                                   (uint32_t)(G.ndy >> tsh) * 2u * B_PART;
             for (int blk = 0; blk < S.nblk; blk++) {
               if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, 1)) { ok = false; break; }
               const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
               if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), PAIR ? 2 * bytes : bytes);
               const uint32_t sa = smem0 + (uint32_t)stage * 2u * STAGE;
-              const int cx = S.c0 + blk * 64, x = ti.j0 + G.dx, y = ti.i0 + G.dy0;
+              const int cx = S.c0 + blk * p.cb, x = ti.j0 + G.dx, y = ti.i0 + G.dy0;
               if constexpr (PAIR) tma_load_5d_pair(sa, &p.amap_u[S.amap], cx, x, y, ti.b, 0, fb);
               else tma_load_5d(sa, &p.amap_u[S.amap], cx, x, y, ti.b, 0, fb);
-              for (int j = 0; j < G.ndy; j++) {
-                const int kb = S.sub0 + G.tap[j] * S.nblk + blk;
+              for (int j = 0; j < (G.ndy >> tsh); j++) {
+                const int kb = (S.sub0 + G.tap[j << tsh] * S.nblk + blk) >> tsh;
                 const uint32_t dst = sa + U_A + (uint32_t)j * 2u * B_PART;
                 if constexpr (PAIR) tma_load_3d_pair(dst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
                 else tma_load_3d(dst, &p.bmap[ti.cls], kb * 64, wrow, 0, fb);
@@ -517,33 +522,43 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           for (int g = 0; g < C.ngroup && ok; g++) {
             const GemmGroup& G = C.grp[g];
             const GemmSeg& S = C.seg[G.seg];
-            const uint32_t rowb = (uint32_t)p.bw * 128u;                    // one pixel row of the box
+            const bool sw64 = p.cb == 32;
+            const uint32_t rowb = (uint32_t)p.bw * (uint32_t)p.cb * 2u;     // one pixel row of the box
             const uint32_t apart = (uint32_t)p.urows[S.amap] * rowb;        // hi part of the box
             for (int blk = 0; blk < S.nblk; blk++) {
               if (!mbar_wait(full_bar(stage), phase, p.err, 3)) { ok = false; break; }
               tc_fence_after();
               const uint32_t sa = smem0 + (uint32_t)stage * 2u * STAGE;
-              for (int j = 0; j < G.ndy; j++) {
-                const uint32_t aj = sa + (uint32_t)j * rowb;
-                const uint32_t bj = sa + U_A + (uint32_t)j * 2u * B_PART;
+              // the K steps of one tap: 64-channel rows (128-byte swizzle) or
+              // 32-channel rows (64-byte swizzle), unrolled per case
+              auto tap_mmas = [&](auto kst) {
+                constexpr int KS = decltype(kst)::value;
+                constexpr uint32_t SBO = KS == 4 ? 1024u : 512u, LAYOUT = KS == 4 ? 2u : 4u;
+                constexpr int TPK = KS == 4 ? 1 : 2;  // taps per K block
+                for (int j = 0; j < G.ndy; j++) {
+                  const uint32_t aj = sa + (uint32_t)j * rowb;
+                  const uint32_t bj = sa + U_A + (uint32_t)(j / TPK) * 2u * B_PART + (uint32_t)(j % TPK) * 64u;
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                  const uint64_t a_hi = smem_desc(aj + k * 32, 1024u, 2u);
-                  const uint64_t a_lo = smem_desc(aj + apart + k * 32, 1024u, 2u);
-                  const uint64_t b_hi = smem_desc(bj + k * 32, 1024u, 2u);
-                  const uint64_t b_lo = smem_desc(bj + B_PART + k * 32, 1024u, 2u);
-                  if constexpr (PAIR) {
-                    mma_bf16_pair(d_tmem, a_lo, b_hi, IDESC, accum);
-                    mma_bf16_pair(d_tmem, a_hi, b_lo, IDESC, 1u);
-                    mma_bf16_pair(d_tmem, a_hi, b_hi, IDESC, 1u);
-                  } else {
-                    mma_bf16(d_tmem, a_lo, b_hi, IDESC, accum);
-                    mma_bf16(d_tmem, a_hi, b_lo, IDESC, 1u);
-                    mma_bf16(d_tmem, a_hi, b_hi, IDESC, 1u);
+                  for (int k = 0; k < KS; k++) {
+                    const uint64_t a_hi = smem_desc(aj + k * 32, SBO, LAYOUT);
+                    const uint64_t a_lo = smem_desc(aj + apart + k * 32, SBO, LAYOUT);
+                    const uint64_t b_hi = smem_desc(bj + k * 32, 1024u, 2u);
+                    const uint64_t b_lo = smem_desc(bj + B_PART + k * 32, 1024u, 2u);
+                    if constexpr (PAIR) {
+                      mma_bf16_pair(d_tmem, a_lo, b_hi, IDESC, accum);
+                      mma_bf16_pair(d_tmem, a_hi, b_lo, IDESC, 1u);
+                      mma_bf16_pair(d_tmem, a_hi, b_hi, IDESC, 1u);
+                    } else {
+                      mma_bf16(d_tmem, a_lo, b_hi, IDESC, accum);
+                      mma_bf16(d_tmem, a_hi, b_lo, IDESC, 1u);
+                      mma_bf16(d_tmem, a_hi, b_hi, IDESC, 1u);
+                    }
+                    accum = 1u;
                   }
-                  accum = 1u;
                 }
-              }
+              };
+              if (sw64) tap_mmas(std::integral_constant<int, 2>{});
+              else tap_mmas(std::integral_constant<int, 4>{});
               if constexpr (PAIR) mma_commit_pair(empty_bar(stage), 3);
               else mma_commit(empty_bar(stage));
               if (++stage == USTAGES) { stage = 0; phase ^= 1; }

@@ -690,12 +690,16 @@ struct Builder {
     // of 4 x 32 pixels; the kernel's union stages exist for 64 B rows per CTA
     // (BN = 64 single CTAs, BN = 128 pairs); split-K launches keep per-tap boxes.
     std::vector<std::vector<GemmGroup>> groups(classes.size());
-    bool uni = !swap && cb == 64 && (pair ? bn == 128 : bn == 64) && mw % 32 == 0 && mh % 4 == 0;
+    // 32-channel boxes (model.1): two taps per K block, so groups are whole K
+    // blocks (2 or 4 consecutive taps of one-block segments)
+    bool uni = !swap && (cb == 64 || cb == 32) && (pair ? bn == 128 : bn == 64) && mw % 32 == 0 && mh % 4 == 0;
+    const int maxrun = cb == 64 ? 3 : 4;
     bool multi = false;
     for (size_t ci = 0; ci < classes.size() && uni; ci++) {
+      int sub_base = 0;  // first cb-channel sub-box of the segment in the class's K order
       for (size_t si = 0; si < classes[ci].segs.size() && uni; si++) {
         const SegSpec& ss = classes[ci].segs[si];
-        if (ss.stride != 1) { uni = false; break; }
+        if (ss.stride != 1 || (cb == 32 && ss.nch != 32)) { uni = false; break; }
         std::vector<int> done(ss.taps.size(), 0);
         for (size_t t0 = 0; t0 < ss.taps.size(); t0 += done[t0] ? 1 : 0) {
           if (done[t0]) continue;
@@ -707,7 +711,7 @@ struct Builder {
           for (size_t t = 0; t < ss.taps.size(); t++)  // start at the smallest dy left in this column
             if (!done[t] && ss.taps[t].second == g.dx) g.dy0 = (int8_t)std::min<int>(g.dy0, ss.taps[t].first);
           g.ndy = 0;
-          for (int d = 0; d < 3; d++) {
+          for (int d = 0; d < maxrun; d++) {
             int found = -1;
             for (size_t t = 0; t < ss.taps.size(); t++)
               if (!done[t] && ss.taps[t].second == g.dx && ss.taps[t].first == g.dy0 + d) found = (int)t;
@@ -715,9 +719,15 @@ struct Builder {
             done[found] = 1;
             g.tap[g.ndy++] = (int8_t)found;
           }
+          if (cb == 32) {  // whole K blocks: an even run of consecutive tap indices starting a block
+            bool whole = g.ndy % 2 == 0 && (sub_base + g.tap[0]) % 2 == 0;
+            for (int j = 1; j < g.ndy; j++) whole = whole && g.tap[j] == g.tap[0] + j;
+            if (!whole) { uni = false; break; }
+          }
           multi = multi || g.ndy > 1;
           groups[ci].push_back(g);
         }
+        sub_base += (ss.nch / cb) * (int)ss.taps.size();
       }
       if (groups[ci].size() > (size_t)GEMM_MAX_GROUPS) uni = false;
     }

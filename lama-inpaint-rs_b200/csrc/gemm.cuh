@@ -48,12 +48,12 @@ struct GemmSeg {
 };
 
 // Row-union mode: taps of one segment that share dx and have consecutive dy
-// (up to 3) form a group; per 64-channel block the group's A tiles are the
-// row windows of ONE box of bh + ndy - 1 rows, loaded once.
+// (up to 3 with 64-channel boxes; 2 or 4 whole K blocks with 32-channel
+// boxes) form a group; per channel block the group's A tiles are the row
+// windows of ONE box of bh + ndy - 1 rows, loaded once.
 struct GemmGroup {
   int8_t seg, dx, dy0, ndy;
-  int8_t tap[3];
-  int8_t pad;
+  int8_t tap[4];
 };
 
 struct GemmClass {
@@ -74,8 +74,8 @@ struct GemmClass {
 struct GemmParams {
   CUtensorMap amap[GEMM_MAX_AMAPS];
   CUtensorMap bmap[GEMM_MAX_CLASSES];
-  // row-union mode (uni = 1; tiles of bh = 4 x bw = 32 pixels, 64-channel
-  // boxes, stride 1, no split-K, BN = 64 or CTA pairs of BN = 128): per A map
+  // row-union mode (uni = 1; tiles of bh = 4 x bw = 32 pixels, 64- or
+  // 32-channel boxes, stride 1, no split-K, BN = 64 or CTA pairs of BN = 128): per A map
   // a map of boxes of urows = bh + (longest group) - 1 rows, both parts
   CUtensorMap amap_u[GEMM_MAX_AMAPS];
   int uni;
