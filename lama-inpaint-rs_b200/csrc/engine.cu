@@ -955,7 +955,7 @@ struct Builder {
         r.f = fp;
         if (pf) {
           r.fpf.reset(new FftPfParams{feat_map, fp});
-          r.grid = std::min(B * 192 / 4, e.sms);
+          r.grid = std::min(B * 192 / 4, 2 * e.sms);  // two CTAs per SM
         }
         r.bytes = px * 192 * 4 + pxs * 384 * 4;
         r.out_ptr = spec.p; r.out_split = 1; r.out_part = spec.part();

@@ -266,12 +266,13 @@ int prepare_pair() {
   return (int)cudaFuncSetAttribute(k_irfft2_reg<H, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
-// ------------------------------------------------------------------ rfft2, prefetching variant (64 x 64)
-// Persistent CTAs (one per SM) walk items = (image, 4 channels).  The item's
-// feat rows (4 x 64 rows of 256 bytes) arrive by TMA, 128-byte swizzled, in one
-// of two shared-memory buffers while the previous item is being transformed,
-// so the row pass reads shared memory and the DRAM traffic of one item
-// overlaps the arithmetic and stores of the other.
+// ------------------------------------------------------------------ rfft2, TMA-fed variant (64 x 64)
+// Persistent CTAs, two per SM, walk items = (image, 4 channels).  The item's
+// feat rows (4 x 64 rows of 256 bytes) arrive by TMA, 128-byte swizzled, in
+// the first 64 KB of the CTA's plane buffer; every thread takes its row into
+// registers, and after a barrier the row transforms overwrite the same bytes
+// with the [c][kx][y] plane.  A CTA loads its next item once its column pass
+// is done; the other CTA on the SM computes meanwhile, which hides the load.
 //   rows: thread (c, y) = (t / 64, t % 64): the row as a 32-point complex
 //     transform + untangling, into the plane [c][kx][y];
 //   columns: thread (c, h, slot) = (t % 4, t / 4 % 2, t / 8): half h (outputs of
@@ -282,48 +283,44 @@ constexpr uint32_t PF_BOX = 256 * 128;    // one TMA box: 256 rows x 32 floats
 constexpr uint32_t PF_BUF = 2 * PF_BOX;   // one item: x in [0, 32) and [32, 64)
 constexpr int PF_KS = 34, PF_YS = 65;     // plane strides (float2)
 constexpr size_t PF_PLANE = (size_t)PF_CG * PF_KS * PF_YS * sizeof(float2);
-constexpr size_t PF_SMEM = 1024 + 2 * PF_BUF + PF_PLANE + 64;
+static_assert(PF_PLANE >= PF_BUF, "the TMA landing zone fits in the plane buffer");
+constexpr size_t PF_SMEM = 1024 + PF_PLANE + 64;
 
-__global__ void __launch_bounds__(256, 1) k_rfft2_pf(const __grid_constant__ FftPfParams q) {
+__global__ void __launch_bounds__(256, 2) k_rfft2_pf(const __grid_constant__ FftPfParams q) {
   constexpr int H = 64, W = 64, WH = 33, HALF = 32;
   const FftParams& p = q.p;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float2* plane = reinterpret_cast<float2*>(smem + 2 * PF_BUF);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * PF_BUF + PF_PLANE);
+  float2* plane = reinterpret_cast<float2*>(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PF_PLANE);
   auto P = [&](int c, int kx, int y) -> float2& { return plane[(c * PF_KS + kx) * PF_YS + y]; };
   const int t = threadIdx.x;
   const int groups = p.c / PF_CG, items = p.batch * groups;
-  auto issue = [&](int item, int s) {
+  auto issue = [&](int item) {
     const int b = item / groups, c0 = (item - b * groups) * PF_CG;
     const int row = (b * p.c + c0) * H;
-    const uint32_t bar = smem_u32(full + s);
+    const uint32_t bar = smem_u32(full);
     mbar_arrive_expect_tx(bar, PF_BUF);
-    tma_load_2d(smem_u32(smem + s * PF_BUF), &q.feat_map, 0, row, bar);
-    tma_load_2d(smem_u32(smem + s * PF_BUF + PF_BOX), &q.feat_map, 32, row, bar);
+    tma_load_2d(smem_u32(smem), &q.feat_map, 0, row, bar);
+    tma_load_2d(smem_u32(smem + PF_BOX), &q.feat_map, 32, row, bar);
   };
   if (t == 0) {
     mbar_init(smem_u32(full), 1);
-    mbar_init(smem_u32(full + 1), 1);
     fence_mbar_init();
     tma_prefetch(&q.feat_map);
+    if (blockIdx.x < items) issue(blockIdx.x);
   }
   __syncthreads();
-  if (t == 0) {
-    for (int s = 0; s < 2; s++)
-      if (blockIdx.x + s * gridDim.x < items) issue(blockIdx.x + s * gridDim.x, s);
-  }
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.spec);
   const int C2 = 2 * p.c;
   int k = 0;
   for (int item = blockIdx.x; item < items; item += gridDim.x, k++) {
-    const int s = k & 1;
-    const bool ok = __syncthreads_and(mbar_wait(smem_u32(full + s), (k >> 1) & 1, p.err, 7));
+    const bool ok = __syncthreads_and(mbar_wait(smem_u32(full), k & 1, p.err, 7));
     if (!ok) break;
     const int b = item / groups, c0 = (item - b * groups) * PF_CG;
     {
       const int c = t >> 6, y = t & 63, r = c * 64 + y;
-      const uint8_t* rowb = smem + s * PF_BUF + r * 128;
+      const uint8_t* rowb = smem + r * 128;
       float2 z[HALF];
 #pragma unroll
       for (int i = 0; i < 16; i++) {
@@ -331,6 +328,7 @@ __global__ void __launch_bounds__(256, 1) k_rfft2_pf(const __grid_constant__ Fft
         z[2 * i] = make_float2(v.x, v.y);
         z[2 * i + 1] = make_float2(v.z, v.w);
       }
+      __syncthreads();  // every row is in registers: the plane may overwrite the landing zone
       fft_reg<HALF, false>(z);
 #pragma unroll
       for (int kx = 0; kx <= HALF; kx++) {
@@ -341,11 +339,7 @@ __global__ void __launch_bounds__(256, 1) k_rfft2_pf(const __grid_constant__ Fft
         P(c, kx, y) = cadd(e, cmul(o, twid<W, false>(kx)));
       }
     }
-    __syncthreads();  // buffer s consumed, plane complete
-    if (t == 0 && item + 2 * gridDim.x < items) {
-      fence_async_smem();
-      issue(item + 2 * gridDim.x, s);
-    }
+    __syncthreads();  // plane complete
     {
       const int c = t & 3, h = (t >> 2) & 1, slot = t >> 3;
       float2 u[HALF];
@@ -360,6 +354,11 @@ __global__ void __launch_bounds__(256, 1) k_rfft2_pf(const __grid_constant__ Fft
           bb = P(c, slot, n + HALF);
         }
         u[n] = h ? cmul(csub(a, bb), twid<H, false>(n)) : cadd(a, bb);
+      }
+      __syncthreads();  // the plane is read: the next item's rows may land in it
+      if (t == 0 && item + gridDim.x < items) {
+        fence_async_smem();
+        issue(item + gridDim.x);
       }
       fft_reg<HALF, false>(u);  // u[k2] = X[2 k2 + h]
       const int cc = c0 + c;
@@ -386,7 +385,6 @@ __global__ void __launch_bounds__(256, 1) k_rfft2_pf(const __grid_constant__ Fft
         for (int k2 = 0; k2 < HALF; k2++) store(2 * k2 + h, slot, u[k2]);
       }
     }
-    __syncthreads();  // plane free for the next item
   }
 }
 
