@@ -476,7 +476,7 @@ void load_weights(const WeightFile& wf, Weights& W) {
 }
 
 // ------------------------------------------------------------------ ops
-enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_IRFFT_PAR, OP_OUTCONV, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_TO_SPLIT, OP_TO_NCHW };
+enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_IRFFT_PAR, OP_OUTCONV, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_TO_SPLIT, OP_TO_NCHW, OP_COPY };
 
 struct Op {
   OpKind kind;
@@ -484,6 +484,9 @@ struct Op {
   int bn = 0, grid = 0;
   std::unique_ptr<GemmParams> g;
   std::unique_ptr<FftPfParams> fpf;
+  const void* csrc = nullptr;  // OP_COPY: device-to-device copy
+  void* cdst = nullptr;
+  size_t cbytes = 0;
   std::unique_ptr<OutConvParams> oc;
   FftParams f{};
   UnfoldParams u{};
@@ -512,6 +515,7 @@ int launch_op(const Op& op, cudaStream_t st) {
     case OP_UNFOLD_U8: return launch_unfold_u8(op.u, st);
     case OP_TO_SPLIT: return launch_nchw_to_split(op.cv, st);
     case OP_TO_NCHW: return launch_split_to_nchw(op.cv, st);
+    case OP_COPY: return (int)cudaMemcpyAsync(op.cdst, op.csrc, op.cbytes, cudaMemcpyDeviceToDevice, st);
   }
   return -1;
 }
@@ -1125,6 +1129,15 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
     }
     pl->ops.push_back(std::move(un));
     if (kind == 1) {
+      // the composite's unmasked bytes are the source bytes: copied whole
+      // here, and the OutConv writes only the masked pixels
+      Op cp;
+      cp.kind = OP_COPY;
+      cp.name = "copy_source";
+      cp.csrc = pl->rgb;
+      cp.cdst = pl->out_rgb;
+      cp.cbytes = (size_t)B * h * w * 3;
+      pl->ops.push_back(std::move(cp));
       const CompositeParams comp{B, h, w, H, W, pl->rgb, pl->mask, nullptr, pl->out_rgb};
       b.core(U, B, H, W, nullptr, &comp);
     } else if (kind == 3) {

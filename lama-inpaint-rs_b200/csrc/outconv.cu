@@ -179,6 +179,22 @@ __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__
           const int rr = base + i;
           if (rr >= nin) break;
           const int a = it & 1;
+          // u8 path: this row's source bytes are loaded before the accumulator
+          // wait, so their latency is hidden by it (used after the row's sums)
+          uint32_t src = 0;  // mask byte << 24
+          bool src_in = false;
+          if (part == 0 && col && rr >= 6 && (q.win || q.dst)) {
+            const int y = y0 + rr - 6, x = x0 + ox;
+            if (q.win) {
+              const WinDesc& d = *q.win;
+              const int gy = d.wy0 + y, gx = d.wx0 + x;
+              src_in = y < q.ih && x < q.iw && gx >= d.sx0 && gx < d.sx1 && gy >= d.sy0 && gy < d.sy1;
+              if (src_in) src = (uint32_t)__ldg(d.mask + (size_t)gy * d.fw + gx) << 24;
+            } else {
+              src_in = y < q.ih && x < q.iw;
+              if (src_in) src = (uint32_t)__ldg(q.mask + ((size_t)b * q.ih + y) * q.iw + x) << 24;
+            }
+          }
           if (ok) ok = mbar_wait(tfull_bar(a), (it >> 1) & 1, q.err, 15);
           ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the shuffles below take every lane
           it++;
@@ -249,8 +265,7 @@ __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__
                 const int y = y0 + yd, x = x0 + ox;
                 const WinDesc& d = *q.win;
                 const int gy = d.wy0 + y, gx = d.wx0 + x;
-                if (y < q.ih && x < q.iw && gx >= d.sx0 && gx < d.sx1 && gy >= d.sy0 && gy < d.sy1 &&
-                    d.mask[(size_t)gy * d.fw + gx] != 0) {
+                if (src_in && (src >> 24) != 0) {
                   uint8_t* o = d.img + ((size_t)gy * d.fw + gx) * 3;
 #pragma unroll
                   for (int co = 0; co < 3; co++) {
@@ -260,15 +275,10 @@ __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__
                 }
               } else if (q.dst) {
                 const int y = y0 + yd, x = x0 + ox;
-                if (y < q.ih && x < q.iw) {
+                if (src_in && (src >> 24) != 0) {  // unmasked bytes were copied from the source
                   const size_t pix = ((size_t)b * q.ih + y) * q.iw + x;
                   uint8_t* d = q.dst + pix * 3;
-                  if (q.mask[pix] == 0) {
-                    const uint8_t* r = q.rgb + pix * 3;
-                    d[0] = r[0];
-                    d[1] = r[1];
-                    d[2] = r[2];
-                  } else {
+                  {
 #pragma unroll
                     for (int co = 0; co < 3; co++) {
                       const float v = fminf(fmaxf(1.0f / (1.0f + expf(-z[co])), 0.0f), 1.0f) * 255.0f;

@@ -17,7 +17,8 @@ struct OutConvParams {
   float* out;         // [B][3][H][W] fp32 (unused when dst is set)
   // Composite + quantise instead of the fp32 store (the u8 path, lama-rs
   // src/main.rs:272-307): for image pixels (y < ih, x < iw) of the padded
-  // output, dst = rgb where mask == 0, else (u8)(int)(clamp(v, 0, 1) * 255 + 0.5);
+  // output where mask != 0, dst = (u8)(int)(clamp(v, 0, 1) * 255 + 0.5); the
+  // plan copies rgb into dst beforehand, which gives the unmasked bytes.
   // rgb / dst [B][ih][iw][3], mask [B][ih][iw].
   const uint8_t* rgb;
   const uint8_t* mask;
