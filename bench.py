@@ -10,8 +10,9 @@ path.  A step is the whole job: every rank inpaints its share (in chunks of
 value : 512^2 inpaints/s for the whole job, inputs already in device memory
         (lama_inpaint_u8_device: input build, forward, composite), device time
         from CUDA events on the engine stream, max over ranks.
-e2e   : the same through the host-buffer API (lama_inpaint_u8): pinned u8
-        rgb+mask host->device, forward, composite, u8 device->host every step.
+e2e   : the same through the host-buffer API (lama_inpaint_u8_stream): pinned
+        u8 rgb+mask host->device, forward, composite, u8 device->host every
+        step, the copies of one chunk overlapping the pass of another.
 roofline : the dominant kernel (the FFC-layer GEMM, ~70 % of the FLOPs) from a
         per-launch CUDA-event profile of one chunk, algorithmic FLOPs (2 x MAC,
         real taps only) over the measured bf16 tensor peak.
@@ -220,11 +221,13 @@ def main():
             eng.inpaint_u8_device(rgb[s].data_ptr(), mask[s].data_ptr(), out[s].data_ptr(), c, SIZE, SIZE)
 
     def step_host():
-        from lama_b200.engine import lib, _up  # noqa
+        # lama_inpaint_u8_stream: the rank's images from pinned host memory in
+        # chunks, host<->device copies of one chunk overlapping the pass of another
+        from lama_b200.engine import lib  # noqa
         import ctypes
-        for s, c in chunks:
-            p = lambda t: ctypes.cast(t[s].data_ptr(), ctypes.POINTER(ctypes.c_uint8))  # noqa: E731
-            eng._check(lib().lama_inpaint_u8(eng.handle, p(rgb_h), p(mask_h), c, SIZE, SIZE, p(out_h)))
+        p = lambda t: ctypes.cast(t.data_ptr(), ctypes.POINTER(ctypes.c_uint8))  # noqa: E731
+        eng._check(lib().lama_inpaint_u8_stream(eng.handle, p(rgb_h), p(mask_h), rgb_h.shape[0], SIZE, SIZE,
+                                                args.chunk, p(out_h)))
 
     def timed(fn, k):
         barrier()
@@ -319,7 +322,7 @@ def main():
                        "parallelism": f"replicas x{world}, no collectives"},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": TOTAL_IMAGES * px * 4, "d2h_bytes_per_step": TOTAL_IMAGES * px * 3,
-                    "api": "lama_inpaint_u8 (host pinned u8 in/out)"},
+                    "api": "lama_inpaint_u8_stream (host pinned u8 in/out, --chunk images per pass, copies overlapping the passes)"},
             "gpu_launches": gpu_launches * world,
             "roofline": roof,
             "cpu_baseline": cb,

@@ -77,6 +77,15 @@ int lama_forward_device(lama_engine* e, const float* d_in, int batch, int h, int
 int lama_inpaint_u8(lama_engine* e, const uint8_t* rgb, const uint8_t* mask, int batch, int h, int w,
                     uint8_t* out_rgb);
 
+/* lama_inpaint_u8 over n images from host memory, `chunk` images per pass,
+ * with the host<->device copies of one chunk overlapping the pass of the
+ * previous one (a copy stream and two staging sets; copies are asynchronous
+ * when rgb, mask and out_rgb are page-locked).  Same bytes as lama_inpaint_u8
+ * on each chunk.  No counterpart in the reference (its engine takes one image
+ * per call); it is the serving form of `infer` + composite for many images. */
+int lama_inpaint_u8_stream(lama_engine* e, const uint8_t* rgb, const uint8_t* mask, int n, int h, int w, int chunk,
+                           uint8_t* out_rgb);
+
 /* Same with device pointers, ordered on the engine's stream. */
 int lama_inpaint_u8_device(lama_engine* e, const uint8_t* d_rgb, const uint8_t* d_mask, int batch, int h, int w,
                            uint8_t* d_out_rgb);

@@ -595,6 +595,12 @@ struct lama_engine {
   int spectral = LAMA_SPECTRAL_AUTO;
   int pair_clusters = 0;  // co-resident CTA-pair clusters (0: no pair tiles)
   std::map<std::tuple<int, int, int, int, int, int, int>, std::unique_ptr<Plan>> plans;
+  // lama_inpaint_u8_stream: copy stream and double-buffered staging
+  cudaStream_t copy_stream = nullptr;
+  DevMem pipe_mem;
+  size_t pipe_bytes = 0;  // bytes of one staging set (rgb + mask + out)
+  uint8_t* pipe_buf[2] = {nullptr, nullptr};
+  cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
   // --sections: the device-resident working image, mask and pass windows
   DevMem sec_mem;
   uint8_t* sec_img = nullptr;
@@ -1337,6 +1343,61 @@ int lama_inpaint_u8_device(lama_engine* e, const uint8_t* d_rgb, const uint8_t* 
   });
 }
 
+int lama_inpaint_u8_stream(lama_engine* e, const uint8_t* rgb, const uint8_t* mask, int n, int h, int w, int chunk,
+                           uint8_t* out_rgb) {
+  return guarded(e, [&] {
+    if (!rgb || !mask || !out_rgb) throw EngineError{LAMA_EINVAL, "null buffer"};
+    if (n < 1 || chunk < 1) throw EngineError{LAMA_EINVAL, "n and chunk must be positive"};
+    check_shape(std::min(n, chunk), h, w, false);
+    const int H = (h + 7) / 8 * 8, W = (w + 7) / 8 * 8;
+    const size_t px = (size_t)h * w;
+    const size_t set = (size_t)chunk * px * 7;  // rgb + mask + out of one chunk
+    if (!e->copy_stream) {
+      CK(cudaStreamCreateWithFlags(&e->copy_stream, cudaStreamNonBlocking));
+      for (int i = 0; i < 2; i++) {
+        CK(cudaEventCreateWithFlags(&e->ev_in[i], cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&e->ev_done[i], cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&e->ev_out[i], cudaEventDisableTiming));
+      }
+    }
+    if (e->pipe_bytes < set) {
+      sync_check(e);
+      CK(cudaStreamSynchronize(e->copy_stream));
+      e->pipe_mem.free_all();
+      e->pipe_bytes = set;
+      for (int i = 0; i < 2; i++) e->pipe_buf[i] = (uint8_t*)e->pipe_mem.alloc(set, false);
+    }
+    // chunk i: host -> staging (copy stream), staging -> plan, graph, plan ->
+    // staging (engine stream), staging -> host (copy stream).  Staging set
+    // i % 2 is refilled only after chunk i - 2 has left it, so the copies of
+    // one chunk overlap the pass of the other.
+    const int nchunks = (n + chunk - 1) / chunk;
+    for (int i = 0; i < nchunks; i++) {
+      const int s = i & 1, b0 = i * chunk, cb = std::min(chunk, n - b0);
+      uint8_t* srgb = e->pipe_buf[s];
+      uint8_t* smask = srgb + (size_t)chunk * px * 3;
+      uint8_t* sout = smask + (size_t)chunk * px;
+      Plan& pl = get_plan(e, 1, cb, H, W, h, w, 18);
+      if (i >= 2) CK(cudaStreamWaitEvent(e->copy_stream, e->ev_out[s], 0));  // set s is free again
+      CK(cudaMemcpyAsync(srgb, rgb + (size_t)b0 * px * 3, (size_t)cb * px * 3, cudaMemcpyHostToDevice, e->copy_stream));
+      CK(cudaMemcpyAsync(smask, mask + (size_t)b0 * px, (size_t)cb * px, cudaMemcpyHostToDevice, e->copy_stream));
+      CK(cudaEventRecord(e->ev_in[s], e->copy_stream));
+      CK(cudaStreamWaitEvent(e->stream, e->ev_in[s], 0));
+      CK(cudaMemcpyAsync(pl.rgb, srgb, (size_t)cb * px * 3, cudaMemcpyDeviceToDevice, e->stream));
+      CK(cudaMemcpyAsync(pl.mask, smask, (size_t)cb * px, cudaMemcpyDeviceToDevice, e->stream));
+      run_plan(e, pl);
+      CK(cudaMemcpyAsync(sout, pl.out_rgb, (size_t)cb * px * 3, cudaMemcpyDeviceToDevice, e->stream));
+      CK(cudaEventRecord(e->ev_done[s], e->stream));
+      CK(cudaStreamWaitEvent(e->copy_stream, e->ev_done[s], 0));
+      CK(cudaMemcpyAsync(out_rgb + (size_t)b0 * px * 3, sout, (size_t)cb * px * 3, cudaMemcpyDeviceToHost,
+                         e->copy_stream));
+      CK(cudaEventRecord(e->ev_out[s], e->copy_stream));
+    }
+    CK(cudaStreamSynchronize(e->copy_stream));
+    sync_check(e);
+  });
+}
+
 int lama_inpaint_sections_u8(lama_engine* e, const uint8_t* rgb, const uint8_t* mask, int w, int h, const int* rects,
                              int n, int side, uint8_t* out_rgb) {
   return guarded(e, [&] {
@@ -1568,6 +1629,13 @@ void lama_close(lama_engine* e) {
   }
   e->plans.clear();
   e->sec_mem.free_all();
+  e->pipe_mem.free_all();
+  for (int i = 0; i < 2; i++) {
+    if (e->ev_in[i]) cudaEventDestroy(e->ev_in[i]);
+    if (e->ev_done[i]) cudaEventDestroy(e->ev_done[i]);
+    if (e->ev_out[i]) cudaEventDestroy(e->ev_out[i]);
+  }
+  if (e->copy_stream) cudaStreamDestroy(e->copy_stream);
   e->wmem.free_all();
   if (e->stream) cudaStreamDestroy(e->stream);
   cudaGetLastError();

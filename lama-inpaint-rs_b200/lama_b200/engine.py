@@ -53,6 +53,8 @@ SIGNATURES = [
     ("lama_forward_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("lama_inpaint_u8", ctypes.c_int, [_vp, _u8p, _u8p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _u8p]),
     ("lama_inpaint_u8_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    ("lama_inpaint_u8_stream", ctypes.c_int, [_vp, _u8p, _u8p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int, _u8p]),
     ("lama_inpaint_sections_u8", ctypes.c_int, [_vp, _u8p, _u8p, ctypes.c_int, ctypes.c_int,
                                                 ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int, _u8p]),
     ("lama_resblocks", ctypes.c_int, [_vp, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -223,6 +225,18 @@ class Engine:
         out = np.empty_like(rgb)
         self._check(lib().lama_inpaint_u8(self._h, _up(rgb), _up(mask), b, h, w, _up(out)))
         return out[0] if single else out
+
+    def inpaint_u8_stream(self, rgb: np.ndarray, mask: np.ndarray, chunk: int) -> np.ndarray:
+        """rgb [n,h,w,3] u8, mask [n,h,w] u8 -> composited u8 RGB, `chunk` images per pass with
+        the host<->device copies of one chunk overlapping the pass of the previous one."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        mask = np.ascontiguousarray(mask, np.uint8)
+        n, h, w, _ = rgb.shape
+        if mask.shape != (n, h, w):
+            raise LamaError(-1, f"mask is {mask.shape} but image is {rgb.shape}")
+        out = np.empty_like(rgb)
+        self._check(lib().lama_inpaint_u8_stream(self._h, _up(rgb), _up(mask), n, h, w, chunk, _up(out)))
+        return out
 
     def inpaint_sections_u8(self, rgb: np.ndarray, mask: np.ndarray, rects, side: int) -> np.ndarray:
         """--sections on the device: rgb [h,w,3] u8, mask [h,w] u8, rects [(x0, y0, x1, y1), ...]

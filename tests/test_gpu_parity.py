@@ -97,6 +97,18 @@ def test_forward_is_deterministic(engine_tamed):
     np.testing.assert_array_equal(engine_tamed.forward(x), engine_tamed.forward(x))
 
 
+def test_streamed_inpaint_equals_per_chunk_calls(engine_tamed):
+    """lama_inpaint_u8_stream (copies overlapping the passes, a ragged last
+    chunk) gives the bytes of lama_inpaint_u8 chunk by chunk."""
+    from lama_b200 import seeded
+    n, h, w, chunk = 7, 72, 88, 3
+    rgb = np.stack([seeded.value_noise(h, w, 70 + i) for i in range(n)])
+    mask = np.stack([seeded.brush_mask(h, w, 70 + i) for i in range(n)])
+    got = engine_tamed.inpaint_u8_stream(rgb, mask, chunk)
+    exp = np.concatenate([engine_tamed.inpaint_u8(rgb[i:i + chunk], mask[i:i + chunk]) for i in range(0, n, chunk)])
+    np.testing.assert_array_equal(got, exp)
+
+
 @pytest.mark.parametrize("h,w,seed", [(64, 64, 31), (61, 77, 32), (96, 40, 33)])
 def test_inpaint_u8_matches_oracle_composite(engine_tamed, oracle_tamed, h, w, seed):
     img, m, x = make_input(h, w, seed)
