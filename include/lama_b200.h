@@ -161,8 +161,8 @@ int lama_debug_run(lama_engine* e, const float* in, int batch, int h, int w, int
 int lama_debug_read(lama_engine* e, int batch, int h, int w, int op, float* out, long long cap, int* dims,
                     char* name);
 
-/* Diagnostic of the failure path (SURVEY failure detection; the reference
- * has no counterpart): launches one CTA that waits on an mbarrier nothing
+/* Diagnostic of the failure path (failure detection; the reference has no
+ * counterpart): launches one CTA that waits on an mbarrier nothing
  * ever arrives on, with a limit of `limit_ms` milliseconds of SM clock
  * instead of the pass kernels' ~1 s.  The wait gives up, records its code in
  * the engine's device status word and returns, so the call reports

@@ -8,7 +8,7 @@ container_ref.safetensors
     repo's writer produces the same bytes from the same tensors and that both
     readers (the Python one and the engine's C++ one) parse it.
 
-Usage: python tests/golden/make_golden.py [/path/to/reference]
+Usage: python tests/golden/make_golden.py /path/to/reference
 """
 
 import importlib.util
@@ -30,7 +30,9 @@ def fixture_tensors():
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference checkout (holds lama-rs/safetensors_light.py)>")
+    ref = sys.argv[1]
     spec = importlib.util.spec_from_file_location("safetensors_light", os.path.join(ref, "lama-rs", "safetensors_light.py"))
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
