@@ -600,7 +600,7 @@ struct lama_engine {
   DevMem pipe_mem;
   size_t pipe_bytes = 0;  // bytes of one staging set (rgb + mask + out)
   uint8_t* pipe_buf[2] = {nullptr, nullptr};
-  cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
+  cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
   // --sections: the device-resident working image, mask and pass windows
   DevMem sec_mem;
   uint8_t* sec_img = nullptr;
@@ -1357,7 +1357,6 @@ int lama_inpaint_u8_stream(lama_engine* e, const uint8_t* rgb, const uint8_t* ma
       for (int i = 0; i < 2; i++) {
         CK(cudaEventCreateWithFlags(&e->ev_in[i], cudaEventDisableTiming));
         CK(cudaEventCreateWithFlags(&e->ev_done[i], cudaEventDisableTiming));
-        CK(cudaEventCreateWithFlags(&e->ev_out[i], cudaEventDisableTiming));
       }
     }
     if (e->pipe_bytes < set) {
@@ -1367,31 +1366,42 @@ int lama_inpaint_u8_stream(lama_engine* e, const uint8_t* rgb, const uint8_t* ma
       e->pipe_bytes = set;
       for (int i = 0; i < 2; i++) e->pipe_buf[i] = (uint8_t*)e->pipe_mem.alloc(set, false);
     }
-    // chunk i: host -> staging (copy stream), staging -> plan, graph, plan ->
-    // staging (engine stream), staging -> host (copy stream).  Staging set
-    // i % 2 is refilled only after chunk i - 2 has left it, so the copies of
-    // one chunk overlap the pass of the other.
+    // Copy stream: H2D(0), H2D(1), D2H(0), H2D(2), D2H(1), ...; engine stream:
+    // per chunk staging -> plan, the pass, plan -> staging.  So chunk i + 1's
+    // upload and chunk i - 1's download run while chunk i is in the pass.
+    // Staging set i % 2 is refilled (H2D(i + 2)) only after D2H(i), which
+    // the copy stream runs first; the pass of chunk i waits for H2D(i), which
+    // the copy stream runs after D2H(i - 2), the set's previous reader.
     const int nchunks = (n + chunk - 1) / chunk;
-    for (int i = 0; i < nchunks; i++) {
-      const int s = i & 1, b0 = i * chunk, cb = std::min(chunk, n - b0);
-      uint8_t* srgb = e->pipe_buf[s];
-      uint8_t* smask = srgb + (size_t)chunk * px * 3;
-      uint8_t* sout = smask + (size_t)chunk * px;
-      Plan& pl = get_plan(e, 1, cb, H, W, h, w, 18);
-      if (i >= 2) CK(cudaStreamWaitEvent(e->copy_stream, e->ev_out[s], 0));  // set s is free again
+    auto set_of = [&](int i, uint8_t*& srgb, uint8_t*& smask, uint8_t*& sout) {
+      srgb = e->pipe_buf[i & 1];
+      smask = srgb + (size_t)chunk * px * 3;
+      sout = smask + (size_t)chunk * px;
+    };
+    auto upload = [&](int i) {
+      uint8_t *srgb, *smask, *sout;
+      set_of(i, srgb, smask, sout);
+      const int b0 = i * chunk, cb = std::min(chunk, n - b0);
       CK(cudaMemcpyAsync(srgb, rgb + (size_t)b0 * px * 3, (size_t)cb * px * 3, cudaMemcpyHostToDevice, e->copy_stream));
       CK(cudaMemcpyAsync(smask, mask + (size_t)b0 * px, (size_t)cb * px, cudaMemcpyHostToDevice, e->copy_stream));
-      CK(cudaEventRecord(e->ev_in[s], e->copy_stream));
+      CK(cudaEventRecord(e->ev_in[i & 1], e->copy_stream));
+    };
+    upload(0);
+    for (int i = 0; i < nchunks; i++) {
+      const int s = i & 1, b0 = i * chunk, cb = std::min(chunk, n - b0);
+      uint8_t *srgb, *smask, *sout;
+      set_of(i, srgb, smask, sout);
+      Plan& pl = get_plan(e, 1, cb, H, W, h, w, 18);
       CK(cudaStreamWaitEvent(e->stream, e->ev_in[s], 0));
       CK(cudaMemcpyAsync(pl.rgb, srgb, (size_t)cb * px * 3, cudaMemcpyDeviceToDevice, e->stream));
       CK(cudaMemcpyAsync(pl.mask, smask, (size_t)cb * px, cudaMemcpyDeviceToDevice, e->stream));
       run_plan(e, pl);
       CK(cudaMemcpyAsync(sout, pl.out_rgb, (size_t)cb * px * 3, cudaMemcpyDeviceToDevice, e->stream));
       CK(cudaEventRecord(e->ev_done[s], e->stream));
+      if (i + 1 < nchunks) upload(i + 1);
       CK(cudaStreamWaitEvent(e->copy_stream, e->ev_done[s], 0));
       CK(cudaMemcpyAsync(out_rgb + (size_t)b0 * px * 3, sout, (size_t)cb * px * 3, cudaMemcpyDeviceToHost,
                          e->copy_stream));
-      CK(cudaEventRecord(e->ev_out[s], e->copy_stream));
     }
     CK(cudaStreamSynchronize(e->copy_stream));
     sync_check(e);
@@ -1633,7 +1643,6 @@ void lama_close(lama_engine* e) {
   for (int i = 0; i < 2; i++) {
     if (e->ev_in[i]) cudaEventDestroy(e->ev_in[i]);
     if (e->ev_done[i]) cudaEventDestroy(e->ev_done[i]);
-    if (e->ev_out[i]) cudaEventDestroy(e->ev_out[i]);
   }
   if (e->copy_stream) cudaStreamDestroy(e->copy_stream);
   e->wmem.free_all();
