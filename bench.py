@@ -50,11 +50,13 @@ def log(*a):
 
 
 def load_peaks():
+    """(bf16 TFLOP/s burst, bf16 TFLOP/s sustained, HBM GB/s, source)."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
-    return 1590.0, 6650.0, "fallback"
+        burst = d.get("bf16_tflops", 1590.0)
+        return burst, d.get("bf16_tflops_sustained", burst), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
 
 
 def make_data(n_distinct, size, seed0=1000):
@@ -273,7 +275,9 @@ def main():
 
     result = None
     if rank == 0:
-        peak_tf, hbm, peak_src = load_peaks()
+        # the profiled launches run back to back inside a ~100 ms pass at the
+        # power-capped clock, so the tensor roofline is the sustained figure
+        burst_tf, peak_tf, hbm, peak_src = load_peaks()
         # per-kernel profile of one chunk (f32 plan, same kernels), CUDA events per launch
         c0 = chunks[0][1]
         xin = torch.rand((c0, 4, SIZE, SIZE), device="cuda")
@@ -293,7 +297,8 @@ def main():
             achieved = dom["flops"] / dom["launches"] / (per_launch_ms / 1e3) / 1e12
             roof = {"bound": "tensor", "kernel": dom["name"], "achieved": achieved, "peak": peak_tf,
                     "unit": "TFLOP/s", "frac": achieved / peak_tf, "traffic": traffic,
-                    "peak_source": f"{peak_src} bf16 dense (burst)", "issued_frac": 3 * achieved / peak_tf,
+                    "peak_source": f"{peak_src} bf16 dense, sustained (power-capped) figure",
+                    "issued_frac": 3 * achieved / peak_tf, "frac_of_burst": achieved / burst_tf,
                     "note": "FP32 parity via three BF16 MMAs per product (split operands); achieved counts "
                             "algorithmic FLOPs once, issued_frac counts the three MMAs"}
         else:
