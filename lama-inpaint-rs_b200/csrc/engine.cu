@@ -1071,7 +1071,6 @@ struct Builder {
       q.out = out;
       q.win = win;
       if (comp) {
-        q.rgb = comp->rgb;
         q.mask = comp->mask;
         q.dst = comp->dst;
         q.ih = comp->h;
@@ -1144,10 +1143,10 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
       cp.cdst = pl->out_rgb;
       cp.cbytes = (size_t)B * h * w * 3;
       pl->ops.push_back(std::move(cp));
-      const CompositeParams comp{B, h, w, H, W, pl->rgb, pl->mask, nullptr, pl->out_rgb};
+      const CompositeParams comp{B, h, w, H, W, pl->rgb, pl->mask, pl->out_rgb};
       b.core(U, B, H, W, nullptr, &comp);
     } else if (kind == 3) {
-      const CompositeParams comp{B, h, w, H, W, nullptr, nullptr, nullptr, nullptr};
+      const CompositeParams comp{B, h, w, H, W, nullptr, nullptr, nullptr};
       b.core(U, B, H, W, nullptr, &comp, pl->win);
     } else {
       b.core(U, B, H, W, pl->out);

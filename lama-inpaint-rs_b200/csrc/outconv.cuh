@@ -19,8 +19,7 @@ struct OutConvParams {
   // src/main.rs:272-307): for image pixels (y < ih, x < iw) of the padded
   // output where mask != 0, dst = (u8)(int)(clamp(v, 0, 1) * 255 + 0.5); the
   // plan copies rgb into dst beforehand, which gives the unmasked bytes.
-  // rgb / dst [B][ih][iw][3], mask [B][ih][iw].
-  const uint8_t* rgb;
+  // dst [B][ih][iw][3], mask [B][ih][iw].
   const uint8_t* mask;
   uint8_t* dst;
   int ih, iw;

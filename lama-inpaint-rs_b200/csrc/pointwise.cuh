@@ -36,7 +36,6 @@ struct CompositeParams {
   int batch, h, w, H, W;
   const uint8_t* rgb;      // [B][h][w][3]
   const uint8_t* mask;     // [B][h][w]
-  const float* net;        // [B][3][H][W] sigmoid output (unused by the fused composite)
   uint8_t* dst;            // [B][h][w][3]
 };
 
