@@ -41,3 +41,17 @@ def test_abi_version_is_callable_without_a_gpu():
 
 def test_last_error_on_null_engine():
     assert engine.lib().lama_last_error(None) == b"null engine"
+
+
+def test_entry_points_refuse_a_null_engine_without_touching_the_gpu():
+    """Every engine entry point returns LAMA_EINVAL (-1) for a null engine
+    before any CUDA call, including the streamed and --sections drivers."""
+    L = engine.lib()
+    u8 = ctypes.c_uint8 * 16
+    buf = u8()
+    p = ctypes.cast(buf, ctypes.POINTER(ctypes.c_uint8))
+    rects = (ctypes.c_int * 4)(0, 0, 2, 2)
+    assert L.lama_inpaint_u8(None, p, p, 1, 2, 2, p) == -1
+    assert L.lama_inpaint_u8_stream(None, p, p, 1, 2, 2, 1, p) == -1
+    assert L.lama_inpaint_sections_u8(None, p, p, 2, 2, rects, 1, 2, p) == -1
+    assert L.lama_synchronize(None) == -1
