@@ -55,3 +55,9 @@ def test_entry_points_refuse_a_null_engine_without_touching_the_gpu():
     assert L.lama_inpaint_u8_stream(None, p, p, 1, 2, 2, 1, p) == -1
     assert L.lama_inpaint_sections_u8(None, p, p, 2, 2, rects, 1, 2, p) == -1
     assert L.lama_synchronize(None) == -1
+
+
+def test_integration_notes_cover_every_declared_entry_point():
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    missing = [n for n in declared_functions() if n not in doc]
+    assert not missing, missing
