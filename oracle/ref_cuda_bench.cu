@@ -23,8 +23,16 @@
 // Weights are seeded pseudo-random values of the big-lama shapes (timing does not
 // depend on them).
 //
-// Usage: ref_cuda_bench [side=512] [passes=5] [warmup=2]; prints one line
-// "ref_cuda side=S ms_per_pass=T passes=K".
+// Usage:
+//   ref_cuda_bench [side=512] [passes=5] [warmup=2]
+//     times passes with seeded pseudo-random weights; prints one line
+//     "ref_cuda side=S ms_per_pass=T passes=K arena_used_gb=G".
+//   ref_cuda_bench --run WEIGHTS.safetensors IN.f32 OUT.f32 H W
+//     one pass with the checkpoint's weights (F32 safetensors, big-lama names,
+//     BN folded as cuda.rs:737-756 folds it, ConvT phase matrices built as
+//     cuda.rs:913-945 builds them) on IN = [4][H][W] f32; writes the sigmoid
+//     output [3][H][W] f32 to OUT.  This is how the tests check the CPU oracle
+//     against the reference's own kernels.
 #include <cuda_runtime.h>
 #include <cufft.h>
 
@@ -32,6 +40,9 @@
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
+#include <map>
+#include <string>
 #include <vector>
 
 #include "lama.cu"
@@ -97,26 +108,118 @@ float* weight(long long n, float amp) {
   h_fill<<<grid_for(n, BLOCK), BLOCK>>>(p, n, g_seed++ * 7919u, amp);
   return p;
 }
+float* upload(const std::vector<float>& v) {
+  float* p;
+  CK(cudaMalloc(&p, v.size() * 4));
+  CK(cudaMemcpy(p, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+  return p;
+}
+
+// F32 safetensors: an 8-byte header length, a JSON header, then the data.
+struct Checkpoint {
+  std::vector<char> bytes;
+  size_t data0 = 0;
+  std::string header;
+  bool open(const char* path) {
+    FILE* f = fopen(path, "rb");
+    if (!f) return false;
+    fseek(f, 0, SEEK_END);
+    bytes.resize((size_t)ftell(f));
+    fseek(f, 0, SEEK_SET);
+    const bool ok = fread(bytes.data(), 1, bytes.size(), f) == bytes.size();
+    fclose(f);
+    if (!ok || bytes.size() < 8) return false;
+    unsigned long long n = 0;
+    memcpy(&n, bytes.data(), 8);
+    if (8 + n > bytes.size()) return false;
+    header.assign(bytes.data() + 8, (size_t)n);
+    data0 = 8 + (size_t)n;
+    return true;
+  }
+  std::vector<float> get(const std::string& name, size_t expect) const {
+    const std::string key = "\"" + name + "\":";
+    const size_t at = header.find(key);
+    if (at == std::string::npos) { fprintf(stderr, "missing tensor %s\n", name.c_str()); exit(1); }
+    const size_t off = header.find("\"data_offsets\"", at);
+    unsigned long long a = 0, b = 0;
+    if (off == std::string::npos || sscanf(header.c_str() + header.find('[', off), "[%llu,%llu]", &a, &b) != 2 ||
+        (b - a) != expect * 4 || data0 + b > bytes.size()) {
+      fprintf(stderr, "bad tensor %s\n", name.c_str());
+      exit(1);
+    }
+    std::vector<float> v(expect);
+    memcpy(v.data(), bytes.data() + data0 + a, (size_t)(b - a));
+    return v;
+  }
+};
+const Checkpoint* g_ckpt = nullptr;
 
 struct Acts { float* p; int c, h, w; long long n() const { return (long long)c * h * w; } };
 struct Conv { float* w; float* bias; float* w_t; int cin, cout, k; };
 struct Bn { float* scale; float* shift; int c; };
 struct ConvT { float* phase[4]; float* bias; int cin, cout; };
 
-Conv conv(int cin, int cout, int k, bool bias = false, bool direct = false) {
-  Conv c{weight((long long)cout * cin * k * k, 1.0f / std::sqrt((float)cin * k * k)), nullptr, nullptr, cin, cout, k};
-  if (bias) c.bias = weight(cout, 0.05f);
-  if (direct) c.w_t = weight((long long)cout * cin * k * k, 1.0f / std::sqrt((float)cin * k * k));
+// A convolution `prefix`.weight [cout][cin][k][k] (and .bias): from the
+// checkpoint when one is loaded, else seeded values.  `direct`: also the
+// [cin][cout][k][k] copy the direct 7x7 kernel reads (cuda.rs:709-723).
+Conv conv(const std::string& prefix, int cin, int cout, int k, bool bias = false, bool direct = false) {
+  const long long n = (long long)cout * cin * k * k;
+  if (!g_ckpt) {
+    Conv c{weight(n, 1.0f / std::sqrt((float)cin * k * k)), nullptr, nullptr, cin, cout, k};
+    if (bias) c.bias = weight(cout, 0.05f);
+    if (direct) c.w_t = weight(n, 1.0f / std::sqrt((float)cin * k * k));
+    return c;
+  }
+  const std::vector<float> w = g_ckpt->get(prefix + ".weight", (size_t)n);
+  Conv c{upload(w), nullptr, nullptr, cin, cout, k};
+  if (bias) c.bias = upload(g_ckpt->get(prefix + ".bias", (size_t)cout));
+  if (direct) {
+    std::vector<float> t((size_t)n);
+    for (int co = 0; co < cout; co++)
+      for (int ci = 0; ci < cin; ci++)
+        for (int q = 0; q < k * k; q++) t[((size_t)ci * cout + co) * k * k + q] = w[((size_t)co * cin + ci) * k * k + q];
+    c.w_t = upload(t);
+  }
   return c;
 }
-Bn bn(int c) { return Bn{weight(c, 0.2f), weight(c, 0.05f), c}; }
+// BatchNorm `prefix` folded to (scale, shift) in f32: s = w / sqrt(var + 1e-5), t = b - mean * s.
+Bn bn(const std::string& prefix, int c) {
+  if (!g_ckpt) return Bn{weight(c, 0.2f), weight(c, 0.05f), c};
+  const auto w = g_ckpt->get(prefix + ".weight", c), b = g_ckpt->get(prefix + ".bias", c);
+  const auto mean = g_ckpt->get(prefix + ".running_mean", c), var = g_ckpt->get(prefix + ".running_var", c);
+  std::vector<float> sc(c), sh(c);
+  for (int i = 0; i < c; i++) {
+    sc[i] = w[i] / std::sqrt(var[i] + 1e-5f);
+    sh[i] = b[i] - mean[i] * sc[i];
+  }
+  return Bn{upload(sc), upload(sh), c};
+}
 const int kTaps[4] = {1, 2, 2, 4};
-ConvT convt(int cin, int cout) {
+// Output-phase tap sets of a k3 s2 p1 transposed conv (cuda.rs:566-577), phase = py * 2 + px.
+const int kTapY[4][4] = {{1, 0, 0, 0}, {1, 1, 0, 0}, {0, 2, 0, 0}, {0, 0, 2, 2}};
+const int kTapX[4][4] = {{1, 0, 0, 0}, {0, 2, 0, 0}, {1, 1, 0, 0}, {0, 2, 0, 2}};
+// ConvT `prefix`.weight [cin][cout][3][3] regrouped into one [cout][cin * taps]
+// matrix per phase, column ci * taps + t (cuda.rs:913-945).
+ConvT convt(const std::string& prefix, int cin, int cout) {
   ConvT t{};
-  for (int ph = 0; ph < 4; ph++) t.phase[ph] = weight((long long)cout * cin * kTaps[ph], 1.0f / std::sqrt(cin * 2.25f));
-  t.bias = weight(cout, 0.05f);
   t.cin = cin;
   t.cout = cout;
+  if (!g_ckpt) {
+    for (int ph = 0; ph < 4; ph++) t.phase[ph] = weight((long long)cout * cin * kTaps[ph], 1.0f / std::sqrt(cin * 2.25f));
+    t.bias = weight(cout, 0.05f);
+    return t;
+  }
+  const auto w = g_ckpt->get(prefix + ".weight", (size_t)cin * cout * 9);
+  for (int ph = 0; ph < 4; ph++) {
+    const int taps = kTaps[ph], k = cin * taps;
+    std::vector<float> m((size_t)cout * k);
+    for (int ci = 0; ci < cin; ci++)
+      for (int ti = 0; ti < taps; ti++)
+        for (int co = 0; co < cout; co++)
+          m[(size_t)co * k + ci * taps + ti] = w[(((size_t)ci * cout + co) * 3 + kTapY[ph][ti]) * 3 + kTapX[ph][ti]];
+    t.phase[ph] = upload(m);
+  }
+  t.bias = upload(g_ckpt->get(prefix + ".bias", cout));
   return t;
 }
 
@@ -176,9 +279,9 @@ Acts view(const Acts& a, int first, int c) { return Acts{a.p + (long long)first 
 struct Spectral { Conv conv1; Bn bn1; Conv fu; Bn fu_bn; Conv conv2; int half; };
 struct FftPlans { int h = 0; cufftHandle r2c = 0, c2r = 0; };
 FftPlans g_fft;
-void fft_plans(int h, int half) {
+void fft_plans(int h, int w, int half) {
   if (g_fft.h == h) return;
-  int n[2] = {h, h};
+  int n[2] = {h, w};
   if (cufftPlanMany(&g_fft.r2c, 2, n, nullptr, 1, 0, nullptr, 1, 0, CUFFT_R2C, half) != CUFFT_SUCCESS ||
       cufftPlanMany(&g_fft.c2r, 2, n, nullptr, 1, 0, nullptr, 1, 0, CUFFT_C2R, half) != CUFFT_SUCCESS) {
     fprintf(stderr, "cufftPlanMany failed\n");
@@ -194,7 +297,7 @@ Acts spectral_forward(const Spectral& sp, const Acts& g) {
   bn_relu(feat, sp.bn1);
   const int h = feat.h, w = feat.w, half = sp.half, hw = w / 2 + 1;
   const float scale = 1.0f / std::sqrt((float)(h * w));
-  fft_plans(h, half);
+  fft_plans(h, w, half);
   float* complex = g_arena.get(2LL * half * h * hw);
   cufftExecR2C(g_fft.r2c, feat.p, (cufftComplex*)complex);
   float* packed = g_arena.get(2LL * half * h * hw);
@@ -270,38 +373,44 @@ struct Net {
   Bn ct_bn[3];
   Conv outc;
 };
-Ffc local_ffc(int cin, int cout, int k, int stride, int pad, bool reflect) {
+Ffc local_ffc(int idx, int cin, int cout, int k, int stride, int pad, bool reflect) {
+  const std::string m = "model." + std::to_string(idx);
   Ffc f{cin, 0, cout, 0, k, stride, pad, reflect};
-  f.l2l = new Conv(conv(cin, cout, k));
-  f.bn_l = new Bn(bn(cout));
+  f.l2l = new Conv(conv(m + ".ffc.convl2l", cin, cout, k));
+  f.bn_l = new Bn(bn(m + ".bn_l", cout));
   return f;
 }
+// The big-lama topology (model.rs:135-257) with the checkpoint's module names.
 Net build_net() {
   Net n;
-  n.m1 = local_ffc(4, 64, 7, 1, 0, false);
-  n.m2 = local_ffc(64, 128, 3, 2, 1, true);
-  n.m3 = local_ffc(128, 256, 3, 2, 1, true);
+  n.m1 = local_ffc(1, 4, 64, 7, 1, 0, false);
+  n.m2 = local_ffc(2, 64, 128, 3, 2, 1, true);
+  n.m3 = local_ffc(3, 128, 256, 3, 2, 1, true);
   n.m4 = Ffc{256, 0, 128, 384, 3, 2, 1, true};
-  n.m4.l2l = new Conv(conv(256, 128, 3));
-  n.m4.l2g = new Conv(conv(256, 384, 3));
-  n.m4.bn_l = new Bn(bn(128));
-  n.m4.bn_g = new Bn(bn(384));
+  n.m4.l2l = new Conv(conv("model.4.ffc.convl2l", 256, 128, 3));
+  n.m4.l2g = new Conv(conv("model.4.ffc.convl2g", 256, 384, 3));
+  n.m4.bn_l = new Bn(bn("model.4.bn_l", 128));
+  n.m4.bn_g = new Bn(bn("model.4.bn_g", 384));
   for (int i = 0; i < 36; i++) {
+    const std::string p = "model." + std::to_string(5 + i / 2) + ".conv" + std::to_string(1 + i % 2);
+    const std::string q = p + ".ffc";
     Ffc f{128, 384, 128, 384, 3, 1, 1, true};
-    f.l2l = new Conv(conv(128, 128, 3));
-    f.l2g = new Conv(conv(128, 384, 3));
-    f.g2l = new Conv(conv(384, 128, 3));
-    f.sp = new Spectral{conv(384, 192, 1), bn(192), conv(384, 384, 1), bn(384), conv(192, 384, 1), 192};
-    f.bn_l = new Bn(bn(128));
-    f.bn_g = new Bn(bn(384));
+    f.l2l = new Conv(conv(q + ".convl2l", 128, 128, 3));
+    f.l2g = new Conv(conv(q + ".convl2g", 128, 384, 3));
+    f.g2l = new Conv(conv(q + ".convg2l", 384, 128, 3));
+    f.sp = new Spectral{conv(q + ".convg2g.conv1.0", 384, 192, 1), bn(q + ".convg2g.conv1.1", 192),
+                        conv(q + ".convg2g.fu.conv_layer", 384, 384, 1), bn(q + ".convg2g.fu.bn", 384),
+                        conv(q + ".convg2g.conv2", 192, 384, 1), 192};
+    f.bn_l = new Bn(bn(p + ".bn_l", 128));
+    f.bn_g = new Bn(bn(p + ".bn_g", 384));
     n.res.push_back(f);
   }
-  const int cins[3] = {512, 256, 128}, couts[3] = {256, 128, 64};
+  const int cins[3] = {512, 256, 128}, couts[3] = {256, 128, 64}, mods[3] = {24, 27, 30};
   for (int u = 0; u < 3; u++) {
-    n.ct[u] = convt(cins[u], couts[u]);
-    n.ct_bn[u] = bn(couts[u]);
+    n.ct[u] = convt("model." + std::to_string(mods[u]), cins[u], couts[u]);
+    n.ct_bn[u] = bn("model." + std::to_string(mods[u] + 1), couts[u]);
   }
-  n.outc = conv(64, 3, 7, true, true);
+  n.outc = conv("model.34", 64, 3, 7, true, true);
   return n;
 }
 
@@ -346,7 +455,52 @@ Acts forward(const Net& net, const Acts& input) {
 
 }  // namespace
 
+int run_file(int argc, char** argv) {
+  if (argc != 7) {
+    fprintf(stderr, "usage: ref_cuda_bench --run WEIGHTS IN.f32 OUT.f32 H W\n");
+    return 2;
+  }
+  const int h = atoi(argv[5]), w = atoi(argv[6]);
+  if (h < 8 || w < 8 || h % 8 || w % 8 || h > 1024 || w > 1024) {
+    fprintf(stderr, "H and W must be multiples of 8 in 8..1024\n");
+    return 2;
+  }
+  static Checkpoint ck;
+  if (!ck.open(argv[2])) {
+    fprintf(stderr, "cannot read %s\n", argv[2]);
+    return 1;
+  }
+  g_ckpt = &ck;
+  std::vector<float> x((size_t)4 * h * w);
+  FILE* f = fopen(argv[3], "rb");
+  if (!f || fread(x.data(), 4, x.size(), f) != x.size()) {
+    fprintf(stderr, "cannot read %s\n", argv[3]);
+    return 1;
+  }
+  fclose(f);
+  CK(cudaStreamCreateWithFlags(&g_st, cudaStreamNonBlocking));
+  g_arena.cap = (size_t)std::max(h, w) * std::max(h, w) * 4 * 16000;
+  CK(cudaMalloc(&g_arena.base, g_arena.cap));
+  Net net = build_net();
+  Acts in{upload(x), 4, h, w};
+  CK(cudaDeviceSynchronize());
+  Acts out = forward(net, in);
+  CK(cudaStreamSynchronize(g_st));
+  CK(cudaGetLastError());
+  std::vector<float> y((size_t)out.n());
+  CK(cudaMemcpy(y.data(), out.p, y.size() * 4, cudaMemcpyDeviceToHost));
+  f = fopen(argv[4], "wb");
+  if (!f || fwrite(y.data(), 4, y.size(), f) != y.size()) {
+    fprintf(stderr, "cannot write %s\n", argv[4]);
+    return 1;
+  }
+  fclose(f);
+  printf("ref_cuda run %dx%d -> %s\n", h, w, argv[4]);
+  return 0;
+}
+
 int main(int argc, char** argv) {
+  if (argc > 1 && strcmp(argv[1], "--run") == 0) return run_file(argc, argv);
   const int side = argc > 1 ? atoi(argv[1]) : 512;
   const int passes = argc > 2 ? atoi(argv[2]) : 5;
   const int warmup = argc > 3 ? atoi(argv[3]) : 2;
