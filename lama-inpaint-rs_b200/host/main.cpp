@@ -161,13 +161,19 @@ struct Engine {
 };
 
 // One window through the engine: build_input + forward + composite on the GPU.
-bool inpaint(Engine& eng, const Rgb8& src, const std::vector<uint8_t>& mask, Rgb8& out, std::string& err) {
+// `oom_hint` names the mode that caps the pass's size; it is added to the
+// message when the device refuses the pass's memory (mem.rs:48-73 refuses
+// such a pass before it starts; here the plan allocates everything before
+// any kernel runs, so the refusal is just as immediate).
+bool inpaint(Engine& eng, const Rgb8& src, const std::vector<uint8_t>& mask, Rgb8& out, std::string& err,
+             const char* oom_hint) {
   out.width = src.width;
   out.height = src.height;
   out.data.resize(src.data.size());
   const int rc = lama_inpaint_u8(eng.e, src.data.data(), mask.data(), 1, src.height, src.width, out.data.data());
   if (rc != 0) {
     err = std::string("gpu inference failed: ") + lama_last_error(eng.e);
+    if (rc == LAMA_ENOMEM) err += std::string(". ") + oom_hint;
     return false;
   }
   return true;
@@ -274,7 +280,11 @@ int run(const Args& a) {
       std::vector<uint8_t> sub_mask = crop_gray(mask, W, x0, y0, side);
       const auto t0 = std::chrono::steady_clock::now();
       Rgb8 filled;
-      if (!inpaint(eng, sub, sub_mask, filled, err)) { log("error: " + err); return 1; }
+      if (!inpaint(eng, sub, sub_mask, filled, err,
+                   "The device cannot hold this window: --sections fills the mask in 512x512 passes.")) {
+        log("error: " + err);
+        return 1;
+      }
       snprintf(msg, sizeof(msg), "inference %dx%d in %.2fs", side, side, secs(t0));
       log(msg);
       out = src;
@@ -286,7 +296,12 @@ int run(const Args& a) {
     }
   } else {
     const auto t0 = std::chrono::steady_clock::now();
-    if (!inpaint(eng, src, mask, out, err)) { log("error: " + err); return 1; }
+    if (!inpaint(eng, src, mask, out, err,
+                 "The device cannot hold this image: --tile runs on a window around the mask, and "
+                 "--sections fills a large mask in 512x512 passes.")) {
+      log("error: " + err);
+      return 1;
+    }
     snprintf(msg, sizeof(msg), "inference %dx%d in %.2fs", W, H, secs(t0));
     log(msg);
   }
