@@ -201,9 +201,9 @@ class Engine:
         single = x.ndim == 3
         if single:
             x = x[None]
-        b, c, h, w = x.shape
-        if c != 4:
-            raise LamaError(-1, f"input must have 4 channels, got {c}")
+        if x.ndim != 4 or x.shape[1] != 4:
+            raise LamaError(-1, f"input must be [4,h,w] or [B,4,h,w] f32, got shape {x.shape}")
+        b, _, h, w = x.shape
         out = np.empty((b, 3, h, w), np.float32)
         self._check(lib().lama_forward(self._h, _fp(x), b, h, w, _fp(out)))
         return out[0] if single else out
@@ -219,6 +219,8 @@ class Engine:
         single = rgb.ndim == 3
         if single:
             rgb, mask = rgb[None], mask[None]
+        if rgb.ndim != 4 or rgb.shape[-1] != 3:
+            raise LamaError(-1, f"rgb must be [h,w,3] or [B,h,w,3] u8, got shape {rgb.shape}")
         b, h, w, _ = rgb.shape
         if mask.shape != (b, h, w):
             raise LamaError(-1, f"mask is {mask.shape[-1]}x{mask.shape[-2]} but image is {w}x{h}")
@@ -231,6 +233,8 @@ class Engine:
         the host<->device copies of one chunk overlapping the pass of the previous one."""
         rgb = np.ascontiguousarray(rgb, np.uint8)
         mask = np.ascontiguousarray(mask, np.uint8)
+        if rgb.ndim != 4 or rgb.shape[-1] != 3:
+            raise LamaError(-1, f"rgb must be [n,h,w,3] u8, got shape {rgb.shape}")
         n, h, w, _ = rgb.shape
         if mask.shape != (n, h, w):
             raise LamaError(-1, f"mask is {mask.shape} but image is {rgb.shape}")
@@ -243,6 +247,8 @@ class Engine:
         (lama_section_rects order), one side x side window per rectangle."""
         rgb = np.ascontiguousarray(rgb, np.uint8)
         mask = np.ascontiguousarray(mask, np.uint8)
+        if rgb.ndim != 3 or rgb.shape[-1] != 3:
+            raise LamaError(-1, f"rgb must be [h,w,3] u8, got shape {rgb.shape}")
         h, w, _ = rgb.shape
         if mask.shape != (h, w):
             raise LamaError(-1, f"mask is {mask.shape[-1]}x{mask.shape[-2]} but image is {w}x{h}")
@@ -263,7 +269,11 @@ class Engine:
         single = l.ndim == 3
         if single:
             l, g = l[None], g[None]
+        if l.ndim != 4 or l.shape[1] != 128:
+            raise LamaError(-1, f"local must be [128,h,w] or [B,128,h,w] f32, got shape {l.shape}")
         b, _, h, w = l.shape
+        if g.shape != (b, 384, h, w):
+            raise LamaError(-1, f"global must be {(b, 384, h, w)} to match local, got {g.shape}")
         lo = np.empty_like(l)
         go = np.empty_like(g)
         self._check(lib().lama_resblocks(self._h, _fp(l), _fp(g), b, h, w, nblocks, _fp(lo), _fp(go)))

@@ -61,3 +61,27 @@ def test_integration_notes_cover_every_declared_entry_point():
     doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
     missing = [n for n in declared_functions() if n not in doc]
     assert not missing, missing
+
+
+def test_binding_rejects_mismatched_shapes_before_calling_the_library():
+    """Wrong shapes would make the library read or write past a host buffer; the
+    binding refuses them first (an engine without a handle: no GPU needed)."""
+    import numpy as np
+    import pytest
+
+    eng = engine.Engine.__new__(engine.Engine)
+    eng._h = None
+    bad = [
+        (eng.forward, (np.zeros((3, 8, 8), np.float32),)),
+        (eng.forward, (np.zeros((8, 8), np.float32),)),
+        (eng.inpaint_u8, (np.zeros((8, 8, 4), np.uint8), np.zeros((8, 8), np.uint8))),
+        (eng.inpaint_u8, (np.zeros((8, 8, 3), np.uint8), np.zeros((8, 9), np.uint8))),
+        (eng.inpaint_u8_stream, (np.zeros((2, 8, 8, 4), np.uint8), np.zeros((2, 8, 8), np.uint8), 1)),
+        (eng.inpaint_sections_u8, (np.zeros((8, 8), np.uint8), np.zeros((8, 8), np.uint8), [], 8)),
+        (eng.resblocks, (np.zeros((128, 8, 8), np.float32), np.zeros((192, 8, 8), np.float32))),
+        (eng.resblocks, (np.zeros((64, 8, 8), np.float32), np.zeros((384, 8, 8), np.float32))),
+    ]
+    for fn, args in bad:
+        with pytest.raises(engine.LamaError) as ex:
+            fn(*args)
+        assert ex.value.code == -1, fn.__name__
