@@ -127,12 +127,30 @@ bool png_decode(const std::vector<uint8_t>& f, const std::string& source, Rgb8& 
   z_stream zs;
   memset(&zs, 0, sizeof(zs));
   if (inflateInit(&zs) != Z_OK) { err = "zlib init failed"; return false; }
-  zs.next_in = idat.data();
-  zs.avail_in = (uInt)idat.size();
-  zs.next_out = raw.data();
-  zs.avail_out = (uInt)raw.size();
-  const int zr = inflate(&zs, Z_FINISH);
-  const size_t got = raw.size() - zs.avail_out;
+  // zlib counts in 32-bit uInt: feed and drain at most 1 GiB per call so that
+  // images whose compressed or raw data exceed 4 GiB are read whole
+  const size_t kStep = size_t(1) << 30;
+  size_t in_pos = 0, out_pos = 0;
+  int zr = Z_OK;
+  while (zr == Z_OK) {
+    if (zs.avail_in == 0 && in_pos < idat.size()) {
+      const size_t n = std::min(kStep, idat.size() - in_pos);
+      zs.next_in = idat.data() + in_pos;
+      zs.avail_in = (uInt)n;
+      in_pos += n;
+    }
+    if (zs.avail_out == 0 && out_pos < raw.size()) {
+      const size_t n = std::min(kStep, raw.size() - out_pos);
+      zs.next_out = raw.data() + out_pos;
+      zs.avail_out = (uInt)n;
+      out_pos += n;
+    }
+    const uInt in_before = zs.avail_in, out_before = zs.avail_out;
+    zr = inflate(&zs, Z_NO_FLUSH);
+    if (zr == Z_OK && zs.avail_in == in_before && zs.avail_out == out_before) break;  // no progress
+    if (zr == Z_BUF_ERROR) break;
+  }
+  const size_t got = out_pos - zs.avail_out;
   inflateEnd(&zs);
   if ((zr != Z_STREAM_END && zr != Z_BUF_ERROR) || got < need) { err = source + ": corrupt image data"; return false; }
 

@@ -94,3 +94,48 @@ def test_png_rejects_low_bit_depth(tmp_path):
     Image.fromarray(np.zeros((4, 4), bool)).save(tmp_path / "b.png")  # 1-bit
     r = run("--decode-png", str(tmp_path / "b.png"), str(tmp_path / "o.png"))
     assert r.returncode == 1 and "bit depth" in r.stderr
+
+
+def _rechunk_idat(png: bytes, piece: int, cut: int = 0) -> bytes:
+    """The same PNG with its compressed stream split into IDAT chunks of `piece`
+    bytes (less its last `cut` bytes), CRCs recomputed."""
+    import struct
+    import zlib
+
+    pos, head, stream, tail = 8, [png[:8]], b"", []
+    while pos < len(png):
+        n = struct.unpack(">I", png[pos:pos + 4])[0]
+        kind, data = png[pos + 4:pos + 8], png[pos + 8:pos + 8 + n]
+        pos += 12 + n
+        if kind == b"IDAT":
+            stream += data
+        else:
+            (tail if stream else head).append(png[pos - 12 - n:pos])
+    stream = stream[:len(stream) - cut]
+    chunks = [stream[i:i + piece] for i in range(0, len(stream), piece)]
+    body = b"".join(struct.pack(">I", len(c)) + b"IDAT" + c + struct.pack(">I", zlib.crc32(b"IDAT" + c))
+                    for c in chunks)
+    return b"".join(head) + body + b"".join(tail)
+
+
+def test_png_stream_split_over_many_idat_chunks(tmp_path):
+    rng = np.random.default_rng(4)
+    im = Image.fromarray(rng.integers(0, 255, (29, 41, 3), dtype=np.uint8))
+    src = tmp_path / "in.png"
+    im.save(src)
+    split = tmp_path / "split.png"
+    split.write_bytes(_rechunk_idat(src.read_bytes(), 97))
+    r = run("--decode-png", str(split), str(tmp_path / "o.png"))
+    assert r.returncode == 0, r.stderr
+    np.testing.assert_array_equal(np.asarray(Image.open(tmp_path / "o.png")), np.asarray(im))
+
+
+def test_png_truncated_stream_is_a_run_error(tmp_path):
+    rng = np.random.default_rng(5)
+    im = Image.fromarray(rng.integers(0, 255, (29, 41, 3), dtype=np.uint8))
+    src = tmp_path / "in.png"
+    im.save(src)
+    bad = tmp_path / "cut.png"
+    bad.write_bytes(_rechunk_idat(src.read_bytes(), 1 << 20, cut=200))
+    r = run("--decode-png", str(bad), str(tmp_path / "o.png"))
+    assert r.returncode == 1 and "corrupt image data" in r.stderr
