@@ -229,7 +229,9 @@ bool png_encode(const Rgb8& img, std::vector<uint8_t>& out, std::string& err) {
   ihdr.push_back(0);
   ihdr.push_back(0);
   chunk("IHDR", ihdr.data(), ihdr.size());
-  chunk("IDAT", z.data(), z.size());
+  // a chunk's length field tops out at 2^31 - 1: the stream goes out in 1 MiB IDAT chunks
+  const size_t kIdat = size_t(1) << 20;
+  for (size_t o = 0; o < z.size(); o += kIdat) chunk("IDAT", z.data() + o, std::min(kIdat, z.size() - o));
   chunk("IEND", nullptr, 0);
   return true;
 }

@@ -139,3 +139,15 @@ def test_png_truncated_stream_is_a_run_error(tmp_path):
     bad.write_bytes(_rechunk_idat(src.read_bytes(), 1 << 20, cut=200))
     r = run("--decode-png", str(bad), str(tmp_path / "o.png"))
     assert r.returncode == 1 and "corrupt image data" in r.stderr
+
+
+def test_png_writer_splits_a_large_stream_into_idat_chunks(tmp_path):
+    """Noise does not compress: a 700x700 image leaves more than one 1 MiB IDAT chunk."""
+    rng = np.random.default_rng(6)
+    im = Image.fromarray(rng.integers(0, 255, (700, 700, 3), dtype=np.uint8))
+    src, dst = tmp_path / "in.png", tmp_path / "out.png"
+    im.save(src)
+    r = run("--decode-png", str(src), str(dst))
+    assert r.returncode == 0, r.stderr
+    assert dst.read_bytes().count(b"IDAT") >= 2
+    np.testing.assert_array_equal(np.asarray(Image.open(dst)), np.asarray(im))
