@@ -131,3 +131,37 @@ def tensor_list() -> list[tuple[str, tuple]]:
     t.append((f"model.{OUTCONV}.weight", (3, 64, 7, 7)))
     t.append((f"model.{OUTCONV}.bias", (3,)))
     return t
+
+
+def algorithmic_flops(h: int, w: int) -> dict[str, float]:
+    """FLOPs of one h x w pass (h, w multiples of 8), 2 x MAC over real taps only:
+    no im2col, padding or transposed-conv zero taps.  Keys: encoder, ffc (the 36
+    FFC layers' 3x3 branches), spectral (their 1x1 convs and FourierUnit convs),
+    decoder (the three ConvTranspose2d), outconv, total."""
+    h8, w8 = h // 8, w // 8
+    f = {}
+    enc = 0
+    ho, wo = h, w  # model.1 is a valid 7x7 over the pad-3 input: output h x w
+    for b in encoder():
+        ho, wo = ho // b.stride, wo // b.stride
+        enc += ho * wo * b.cout * b.cin * b.kernel * b.kernel
+    f["encoder"] = 2.0 * enc
+    ffc = spec = 0
+    for pair in resblocks():
+        for b in pair:
+            taps = b.kernel * b.kernel
+            ffc += h8 * w8 * taps * (b.out_local * b.in_local + b.out_global * b.in_local + b.out_local * b.in_global)
+            half = b.out_global // 2
+            spec += h8 * w8 * (half * b.in_global + b.out_global * half)       # conv1, conv2
+            spec += h8 * (w8 // 2 + 1) * (2 * half) * (2 * half)                # FourierUnit 1x1
+    f["ffc"] = 2.0 * ffc
+    f["spectral"] = 2.0 * spec
+    dec = 0
+    hin, win = h8, w8
+    for _, _, cin, cout in UPSAMPLES:
+        dec += cin * cout * 9 * hin * win
+        hin, win = 2 * hin, 2 * win
+    f["decoder"] = 2.0 * dec
+    f["outconv"] = 2.0 * h * w * 3 * 64 * 49
+    f["total"] = f["encoder"] + f["ffc"] + f["spectral"] + f["decoder"] + f["outconv"]
+    return f
