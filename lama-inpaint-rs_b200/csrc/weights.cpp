@@ -42,7 +42,11 @@ struct Json {
     if (i < s.size() && s[i] == '-') { neg = true; i++; }
     if (i >= s.size() || s[i] < '0' || s[i] > '9') return false;
     v = 0;
-    while (i < s.size() && s[i] >= '0' && s[i] <= '9') v = v * 10 + (s[i++] - '0');
+    while (i < s.size() && s[i] >= '0' && s[i] <= '9') {
+      const int d = s[i++] - '0';
+      if (v > (INT64_MAX - d) / 10) return false;  // does not fit int64: malformed for this container
+      v = v * 10 + d;
+    }
     if (neg) v = -v;
     return true;
   }
@@ -130,7 +134,13 @@ bool WeightFile::open(const std::string& path, std::string& err) {
         return false;
       }
       int64_t numel = 1;
-      for (int64_t d : r.shape) numel *= d;
+      for (int64_t d : r.shape) {
+        if (d < 0 || (d > 0 && numel > INT64_MAX / 4 / d)) {
+          err = "tensor " + name + ": shape has a negative or oversized dimension";
+          return false;
+        }
+        numel *= d;
+      }
       if ((int64_t)(offs[1] - offs[0]) != numel * 4) {
         err = "tensor " + name + ": payload size does not match its shape";
         return false;

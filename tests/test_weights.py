@@ -127,3 +127,22 @@ def test_header_length_past_end_is_rejected(tmp_path):
     p.write_bytes(struct.pack("<Q", 1 << 40) + b"{}")
     e = _engine_error(str(p))
     assert e.code == -2
+
+
+def _raw_container(tmp_path, shape_json, offsets=(0, 16)):
+    import json as _json
+    header = '{"t": {"dtype": "F32", "shape": %s, "data_offsets": [%d, %d]}}' % (shape_json, *offsets)
+    _json.loads(header)  # well-formed JSON; only the numbers are hostile
+    p = tmp_path / "hostile.safetensors"
+    p.write_bytes(struct.pack("<Q", len(header)) + header.encode() + b"\0" * offsets[1])
+    return str(p)
+
+
+@pytest.mark.parametrize("shape_json,msg", [
+    ("[99999999999999999999999]", "bad shape"),           # does not fit int64
+    ("[-1, -4]", "negative or oversized dimension"),       # product 4 matches the payload
+    ("[4611686018427387904, 4]", "negative or oversized dimension"),  # product overflows
+])
+def test_hostile_shapes_are_rejected_without_overflow(tmp_path, shape_json, msg):
+    e = _engine_error(_raw_container(tmp_path, shape_json))
+    assert e.code == -2 and msg in e.msg
