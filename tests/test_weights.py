@@ -146,3 +146,13 @@ def _raw_container(tmp_path, shape_json, offsets=(0, 16)):
 def test_hostile_shapes_are_rejected_without_overflow(tmp_path, shape_json, msg):
     e = _engine_error(_raw_container(tmp_path, shape_json))
     assert e.code == -2 and msg in e.msg
+
+
+def test_a_valid_checkpoint_passes_every_weight_check_before_the_device(weights_baseline):
+    """Parsing, name/shape checks, BN folding and repacking all run on the host
+    before any CUDA call, so without a GPU the first error is the device's."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: the engine would open")
+    e = _engine_error(weights_baseline)
+    assert e.code == -3, e.msg
