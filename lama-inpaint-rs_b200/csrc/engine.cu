@@ -19,6 +19,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <cmath>
@@ -1230,6 +1231,27 @@ void check_shape(int batch, int h, int w, bool mult8) {
     throw EngineError{LAMA_EINVAL, "h and w must be multiples of 8 (the generator has three stride-2 stages)"};
 }
 
+// An op launched on its own (profiling and debug runs, not the captured
+// graph) inside an NVTX range named after the op, so a profiler can pick
+// layers out (`ncu --nvtx --nvtx-include "ffc_out/"`); with no tool attached
+// the range calls do nothing.
+int launch_named(const Op& op, cudaStream_t st) {
+  nvtxRangePushA(op.name.c_str());
+  const int r = launch_op(op, st);
+  nvtxRangePop();
+  return r;
+}
+
+// Events destroyed on every exit path, the error ones included.
+struct EventSet {
+  std::vector<cudaEvent_t> ev;
+  explicit EventSet(size_t n) : ev(n, nullptr) {}
+  ~EventSet() {
+    for (cudaEvent_t x : ev)
+      if (x) cudaEventDestroy(x);
+  }
+};
+
 }  // namespace
 
 extern "C" {
@@ -1529,11 +1551,12 @@ int lama_profile_forward(lama_engine* e, const float* d_in, int batch, int h, in
     Plan& pl = get_plan(e, 0, batch, h, w, h, w, 18);
     const size_t nin = (size_t)batch * 4 * h * w, nout = (size_t)batch * 3 * h * w;
     CK(cudaMemcpyAsync(pl.in_f32, d_in, nin * 4, cudaMemcpyDeviceToDevice, e->stream));
-    std::vector<cudaEvent_t> ev(pl.ops.size() + 1);
+    EventSet evs(pl.ops.size() + 1);
+    std::vector<cudaEvent_t>& ev = evs.ev;
     for (auto& x : ev) CK(cudaEventCreate(&x));
     CK(cudaEventRecord(ev[0], e->stream));
     for (size_t i = 0; i < pl.ops.size(); i++) {
-      CKL(launch_op(pl.ops[i], e->stream));
+      CKL(launch_named(pl.ops[i], e->stream));
       CK(cudaEventRecord(ev[i + 1], e->stream));
     }
     CK(cudaMemcpyAsync(d_out, pl.out, nout * 4, cudaMemcpyDeviceToDevice, e->stream));
@@ -1556,7 +1579,6 @@ int lama_profile_forward(lama_engine* e, const float* d_in, int batch, int h, in
       s.flops += pl.ops[i].flops;
       s.bytes += pl.ops[i].bytes;
     }
-    for (auto& x : ev) cudaEventDestroy(x);
     int n = 0;
     for (const std::string& nm : names) {
       if (n < max_stats && stats) stats[n] = agg[nm];
@@ -1602,7 +1624,7 @@ int lama_debug_run(lama_engine* e, const float* in, int batch, int h, int w, int
     Plan& pl = get_plan(e, 0, batch, h, w, h, w, 18);
     CK(cudaMemcpyAsync(pl.in_f32, in, (size_t)batch * 4 * h * w * 4, cudaMemcpyHostToDevice, e->stream));
     const int n = std::min<int>(n_ops, (int)pl.ops.size());
-    for (int i = 0; i < n; i++) CKL(launch_op(pl.ops[i], e->stream));
+    for (int i = 0; i < n; i++) CKL(launch_named(pl.ops[i], e->stream));
     sync_check(e);
   });
 }
