@@ -1,5 +1,6 @@
-// Timing harness for the reference's CUDA path on a B200 (measurement only:
-// nothing here is part of the engine, and no test depends on it).
+// Harness for the reference's CUDA path on a B200: times it, and runs it on
+// given weights and inputs so the tests can check the CPU oracle against it.
+// Test and measurement infrastructure only: nothing here is part of the engine.
 //
 // The reference's own kernel file (lama-rs/cuda/lama.cu) is compiled into this
 // translation unit from where it lies in the reference checkout (the oracle
