@@ -24,6 +24,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -1232,10 +1233,13 @@ void check_shape(int batch, int h, int w, bool mult8) {
 }
 
 // An op launched on its own (profiling and debug runs, not the captured
-// graph) inside an NVTX range named after the op, so a profiler can pick
-// layers out (`ncu --nvtx --nvtx-include "ffc_out/"`); with no tool attached
-// the range calls do nothing.
+// graph).  With LAMA_NVTX set in the environment it runs inside an NVTX range
+// named after the op, so a profiler can pick layers out
+// (`LAMA_NVTX=1 ncu --nvtx --nvtx-include "ffc_out/" ...`); without it no NVTX
+// call is made.
 int launch_named(const Op& op, cudaStream_t st) {
+  static const bool nvtx = std::getenv("LAMA_NVTX") != nullptr;
+  if (!nvtx) return launch_op(op, st);
   nvtxRangePushA(op.name.c_str());
   const int r = launch_op(op, st);
   nvtxRangePop();
