@@ -103,16 +103,18 @@ struct DevMem {
 };
 
 // ------------------------------------------------------------------ tensor maps
+// Resolved once per process.  A function-local static is initialised once even
+// when engines on several devices are opened from several threads at a time
+// (and is tried again on the next call if resolving it threw).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
     cudaDriverEntryPointQueryResult q;
     void* p = nullptr;
     CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
     if (q != cudaDriverEntryPointSuccess || !p)
       throw EngineError{LAMA_ECUDA, "cuTensorMapEncodeTiled is not available from the driver"};
-    fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
-  }
+    return (PFN_cuTensorMapEncodeTiled_v12000)p;
+  }();
   return fn;
 }
 
