@@ -156,3 +156,29 @@ def test_a_valid_checkpoint_passes_every_weight_check_before_the_device(weights_
         pytest.skip("a GPU is present: the engine would open")
     e = _engine_error(weights_baseline)
     assert e.code == -3, e.msg
+
+
+def test_engines_open_from_several_threads_at_once(weights_baseline):
+    """Engines on different devices may be opened and driven from different
+    threads: the host side of lama_open keeps no process-wide state, so four
+    concurrent opens each get their own engine and their own error text
+    (ctypes releases the GIL around the call)."""
+    import threading
+
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: the engines would open")
+    errs = [None] * 4
+
+    def one(i):
+        try:
+            errs[i] = _engine_error(weights_baseline)
+        except BaseException as x:  # recorded and checked below
+            errs[i] = x
+
+    ts = [threading.Thread(target=one, args=(i,)) for i in range(4)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert all(getattr(e, "code", None) == -3 for e in errs), errs
