@@ -119,23 +119,24 @@ class ClockSampler:
 
 
 def cpu_baseline(weights_path, threads=0):
-    """The oracle on a bounded sample: one 256x256 pass (1/4 of a 512^2 pass's work)."""
+    """The oracle on a bounded sample: one 256x512 pass (half of a 512^2 pass's work,
+    latent 32x64: power-of-two FFTs like the workload's), ~8-12 s on 16 host threads."""
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     from lama_b200 import seeded
     cores = O.set_threads(threads if threads > 0 else (os.cpu_count() or 1))
     orc = O.Oracle(weights_path)
-    side = 256
-    img = seeded.value_noise(side, side, 77)
-    m = seeded.brush_mask(side, side, 77)
+    sh, sw = SIZE // 2, SIZE
+    img = seeded.value_noise(sh, sw, 77)
+    m = seeded.brush_mask(sh, sw, 77)
     x = O.build_input(img, m, 0, 0)
     t0 = time.perf_counter()
     orc.forward(x)
     dt = time.perf_counter() - t0
-    scale = (side * side) / (SIZE * SIZE)
+    scale = (sh * sw) / (SIZE * SIZE)
     return {"value": scale / dt, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"one {side}x{side} forward pass of the C++ restatement of lama-rs/src/cpu.rs "
+            "sample": f"one {sh}x{sw} forward pass of the C++ restatement of lama-rs/src/cpu.rs "
                       f"({dt:.2f} s), scaled by pixel count to 512^2 images/s"}
 
 
