@@ -3,7 +3,11 @@
 These restate, case for case, the reference CLI's own unit tests
 (lama-rs/src/main.rs:801-1158) against this repo's implementation
 (lama-inpaint-rs_b200/host/geometry.cpp): the expected windows, section
-counts and orders below are the reference tests' known answers.
+counts and orders below are the reference tests' known answers.  The one
+reference test not restated here, crop_helpers_copy_the_requested_region, checks
+CLI-internal crop helpers; their counterparts in host/main.cpp are exercised by
+the GPU test of --tile (tests/test_gpu_cli.py), which compares the pasted window
+with the oracle pixel for pixel.
 """
 
 import numpy as np
