@@ -7,7 +7,7 @@ counts and orders below are the reference tests' known answers.  The one
 reference test not restated here, crop_helpers_copy_the_requested_region, checks
 CLI-internal crop helpers; their counterparts in host/main.cpp are exercised by
 the GPU test of --tile (tests/test_gpu_cli.py), which compares the pasted window
-with the oracle pixel for pixel.
+with the oracle pixel by pixel (within one level).
 """
 
 import numpy as np
