@@ -85,3 +85,31 @@ def test_binding_rejects_mismatched_shapes_before_calling_the_library():
         with pytest.raises(engine.LamaError) as ex:
             fn(*args)
         assert ex.value.code == -1, fn.__name__
+
+
+def test_header_is_plain_c_and_links_against_the_library(tmp_path):
+    """A C caller (the reference's FFI side is C-ABI) compiles against the header
+    with a strict C99 compiler and links the library; the program calls an entry
+    point that needs no GPU."""
+    import shutil
+    import subprocess
+    import pytest
+
+    if not shutil.which("gcc"):
+        pytest.skip("no C compiler")
+    inc = os.path.join(ROOT, "include")
+    libdir = os.path.dirname(engine.LIB_PATH)
+    src = tmp_path / "caller.c"
+    src.write_text('#include "lama_b200.h"\n'
+                   "int main(void) {\n"
+                   "  lama_engine* e = 0;\n"
+                   "  if (lama_open(0, 0, &e) != LAMA_EINVAL) return 2;\n"
+                   "  lama_close(e);\n"
+                   "  return lama_abi_version() == 1 ? 0 : 1;\n"
+                   "}\n")
+    exe = tmp_path / "caller"
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", inc, str(src),
+                        "-L", libdir, "-llama_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert subprocess.run([str(exe)]).returncode == 0
