@@ -113,3 +113,23 @@ def test_header_is_plain_c_and_links_against_the_library(tmp_path):
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     assert subprocess.run([str(exe)]).returncode == 0
+
+
+def test_a_missing_library_fails_loudly(tmp_path):
+    """No silent fallback: without liblama_b200.so the binding raises at its
+    first use instead of computing anything another way."""
+    import subprocess
+    import sys
+
+    code = ("import sys; sys.path.insert(0, sys.argv[1])\n"
+            "from lama_b200 import engine\n"
+            "try:\n"
+            "    engine.lib()\n"
+            "except OSError as x:\n"
+            "    print('raised:', x)\n"
+            "    sys.exit(0)\n"
+            "sys.exit(1)\n")
+    env = dict(os.environ, LAMA_B200_LIB=str(tmp_path / "absent.so"))
+    r = subprocess.run([sys.executable, "-c", code, os.path.join(ROOT, "lama-inpaint-rs_b200")], env=env,
+                       capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and "is missing" in r.stdout, r.stdout + r.stderr
