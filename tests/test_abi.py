@@ -133,3 +133,19 @@ def test_a_missing_library_fails_loudly(tmp_path):
     r = subprocess.run([sys.executable, "-c", code, os.path.join(ROOT, "lama-inpaint-rs_b200")], env=env,
                        capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and "is missing" in r.stdout, r.stdout + r.stderr
+
+
+def test_the_product_never_reaches_the_oracle():
+    """The oracle is test infrastructure: nothing in the engine package (CUDA
+    sources, C ABI, CLI, Python binding) imports, links or names it."""
+    pkg = os.path.join(ROOT, "lama-inpaint-rs_b200")
+    hits = []
+    for d, _, files in os.walk(pkg):
+        if "_build" in d:
+            continue
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".cpp", ".h", "Makefile")) or f == "Makefile":
+                txt = open(os.path.join(d, f), errors="replace").read()
+                if re.search(r"\boracle\b", txt):
+                    hits.append(os.path.join(d, f))
+    assert not hits, hits
