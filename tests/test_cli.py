@@ -151,3 +151,34 @@ def test_png_writer_splits_a_large_stream_into_idat_chunks(tmp_path):
     assert r.returncode == 0, r.stderr
     assert dst.read_bytes().count(b"IDAT") >= 2
     np.testing.assert_array_equal(np.asarray(Image.open(dst)), np.asarray(im))
+
+
+def _png16(samples: np.ndarray, ctype: int) -> bytes:
+    """A 16-bit PNG written by hand: samples [h, w, channels] uint16, filter 0."""
+    import struct
+    import zlib
+
+    h, w, _ = samples.shape
+    rows = b"".join(b"\0" + samples[y].astype(">u2").tobytes() for y in range(h))
+
+    def chunk(kind, data):
+        return struct.pack(">I", len(data)) + kind + data + struct.pack(">I", zlib.crc32(kind + data))
+
+    ihdr = struct.pack(">IIBBBBB", w, h, 16, ctype, 0, 0, 0)
+    return (b"\x89PNG\r\n\x1a\n" + chunk(b"IHDR", ihdr) + chunk(b"IDAT", zlib.compress(rows)) +
+            chunk(b"IEND", b""))
+
+
+@pytest.mark.parametrize("ctype,channels", [(2, 3), (6, 4), (4, 2)])
+def test_sixteen_bit_colour_keeps_the_high_byte(tmp_path, ctype, channels):
+    """image.rs:80-120 reads 16-bit samples through their high byte; grey (and
+    grey+alpha) spreads to all three channels, alpha is dropped."""
+    rng = np.random.default_rng(7 + ctype)
+    s = rng.integers(0, 65536, (13, 17, channels), dtype=np.uint16)
+    src = tmp_path / "in16.png"
+    src.write_bytes(_png16(s, ctype))
+    r = run("--decode-png", str(src), str(tmp_path / "o.png"))
+    assert r.returncode == 0, r.stderr
+    hi = (s >> 8).astype(np.uint8)
+    exp = hi[..., :3] if channels >= 3 else np.repeat(hi[..., :1], 3, axis=2)
+    np.testing.assert_array_equal(np.asarray(Image.open(tmp_path / "o.png")), exp)
