@@ -182,3 +182,25 @@ def test_sixteen_bit_colour_keeps_the_high_byte(tmp_path, ctype, channels):
     hi = (s >> 8).astype(np.uint8)
     exp = hi[..., :3] if channels >= 3 else np.repeat(hi[..., :1], 3, axis=2)
     np.testing.assert_array_equal(np.asarray(Image.open(tmp_path / "o.png")), exp)
+
+
+def test_palette_index_past_the_palette_takes_its_last_entry(tmp_path):
+    """image.rs:103-110: an index beyond the palette is clamped to its last entry."""
+    import struct
+    import zlib
+
+    idx = np.array([[0, 1, 2, 5], [5, 1, 0, 3]], np.uint8)
+    pal = bytes([10, 20, 30, 200, 100, 50])  # two entries
+    rows = b"".join(b"\0" + idx[y].tobytes() for y in range(idx.shape[0]))
+
+    def chunk(kind, data):
+        return struct.pack(">I", len(data)) + kind + data + struct.pack(">I", zlib.crc32(kind + data))
+
+    png = (b"\x89PNG\r\n\x1a\n" + chunk(b"IHDR", struct.pack(">IIBBBBB", 4, 2, 8, 3, 0, 0, 0)) +
+           chunk(b"PLTE", pal) + chunk(b"IDAT", zlib.compress(rows)) + chunk(b"IEND", b""))
+    src = tmp_path / "pal.png"
+    src.write_bytes(png)
+    r = run("--decode-png", str(src), str(tmp_path / "o.png"))
+    assert r.returncode == 0, r.stderr
+    table = np.array([[10, 20, 30], [200, 100, 50]], np.uint8)
+    np.testing.assert_array_equal(np.asarray(Image.open(tmp_path / "o.png")), table[np.minimum(idx, 1)])
