@@ -7,10 +7,14 @@
 //
 // Parity status: the reference ships no golden vectors and its Rust engine
 // cannot be built offline (no cargo, and the `lightgpu` git dependency is not
-// vendored), so this restatement is pinned against an independent PyTorch
-// restatement (oracle/torch_ref.py) and against torch.fft, not against outputs
-// of the reference itself: network parity is "parity unpinned" in the sense
-// that no reference-produced number anchors it.
+// vendored).  This restatement is pinned against an independent PyTorch
+// restatement (oracle/torch_ref.py), against torch.fft, and against the
+// reference's own CUDA kernels: oracle/ref_cuda_bench.cu compiles
+// lama-rs/cuda/lama.cu from the reference checkout and runs it in the launch
+// order of cuda::run with the same weights (only the absent toolkit's FFT and
+// elementwise kernels are stand-ins); full passes agree to 1e-4
+// (tests/test_gpu_ref_cuda.py).  No reference-written output file exists to
+// compare against.
 //
 // Arithmetic follows cpu.rs exactly so that it should be bit-identical to the
 // Rust engine:
