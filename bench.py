@@ -20,6 +20,9 @@ roofline : the dominant kernel (the FFC-layer GEMM, ~70 % of the FLOPs) from a
         real taps only) over the measured bf16 tensor peak.
 cpu_baseline : the oracle (C++ restatement of the reference CPU engine,
         OpenMP on all host threads) on a bounded sample, rank 0 at N=1.
+ms_per_1024_pass, extra : batch-1 pass latencies (512^2, 1024^2, 600^2 tile,
+        2048^2, the 18-block stack; graph replay, CUDA events), rank 0 at N=1
+        after the timed region.
 
 --impl reference times that CPU restatement as the reference arm (the
 reference's Rust engine cannot be built here: no cargo, no network).
@@ -176,7 +179,9 @@ def main():
     # pass than at 32 (measured +1.3 % images/s at the power-capped clock, ~3 % fewer cycles)
     ap.add_argument("--chunk", type=int, default=64, help="images per engine call")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--extra", action="store_true", help="also time 1024^2 / stack / tile passes")
+    ap.add_argument("--extra", action="store_true",
+                    help="time the batch-1 passes (512^2, 1024^2, 600^2 tile, 2048^2, 18-block stack) at any N; "
+                         "at N=1 they are always timed")
     ap.add_argument("--single-pass", type=int, default=0, metavar="B",
                     help="run one B-image inpaint pass and exit (the case ncu captures)")
     ap.add_argument("--size", type=int, default=SIZE, help="image side of --single-pass")
@@ -320,7 +325,9 @@ def main():
             except Exception as ex:  # the baseline is reported, never required
                 cb = {"error": str(ex)}
         extra = {}
-        if args.extra:
+        if args.extra or world == 1:
+            # BASELINE's metric also names the ms of one 1024^2 pass: timed on
+            # every single-GPU run, after the timed region
             extra = extra_timings(eng, stream)
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -339,6 +346,7 @@ def main():
             "cpu_baseline": cb,
             "clocks": clk,
             "gflop_per_image": GFLOP_512,
+            "ms_per_1024_pass": extra.get("ms_per_1024_pass_b1"),
             "extra": extra,
         }
     eng.close()
