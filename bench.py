@@ -2,12 +2,11 @@
 """Benchmark of the B200 big-lama engine (driver contract: one JSON line).
 
 Workload: 256 independent 512x512 image/mask pairs
-(seeded value-noise images, 15-35 % brush-stroke masks) on every GPU, one
-process per GPU, weights replicated, no collectives on the data path: the
-images are independent units, so N GPUs run N replicas of the job (weak
-scaling, 256 x N images per step).  A step is the whole job: every rank
-inpaints its 256 images (in chunks of --chunk images per engine call).
-Weights are the seeded BASELINE init.
+(seeded value-noise images, 15-35 % brush-stroke masks) partitioned
+round-robin across the N GPUs, one process per GPU, weights replicated, no
+collectives on the data path (strong scaling: 256/N images per GPU).  A step
+is the whole job: every rank inpaints its share (in chunks of --chunk images
+per engine call).  Weights are the seeded BASELINE init.
 
 value : 512^2 inpaints/s for the whole job, inputs already in device memory
         (lama_inpaint_u8_device: input build, forward, composite), device time
@@ -15,6 +14,7 @@ value : 512^2 inpaints/s for the whole job, inputs already in device memory
 e2e   : the same through the host-buffer API (lama_inpaint_u8_stream): pinned
         u8 rgb+mask host->device, forward, composite, u8 device->host every
         step, the copies of one chunk overlapping the pass of another.
+weak  : (N > 1) the same job with 256 images on EVERY rank, for comparison.
 roofline : the dominant kernel (the FFC-layer GEMM, ~70 % of the FLOPs) from a
         per-launch CUDA-event profile of one chunk, algorithmic FLOPs (2 x MAC,
         real taps only) over the measured bf16 tensor peak.
@@ -25,7 +25,10 @@ ms_per_1024_pass, extra : batch-1 pass latencies (512^2, 1024^2, 600^2 tile,
         after the timed region.
 
 --impl reference times that CPU restatement as the reference arm (the
-reference's Rust engine cannot be built here: no cargo, no network).
+reference's Rust engine cannot be built here: no cargo, no network) and, at
+N=1 where the harness was built, the reference's own CUDA kernels
+(oracle/_ref/ref_cuda_bench: lama-rs/cuda/lama.cu in cuda::run's launch order)
+on one 512^2 and one 1024^2 image per pass.
 """
 
 from __future__ import annotations
@@ -42,10 +45,10 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "lama-inpaint-rs_b200"))
 
-IMAGES_PER_RANK = 256
+IMAGES_TOTAL = 256
 SIZE = 512
 N_DISTINCT = 8
-METRIC = "512^2 inpaints/sec (256 independent 512x512 image/mask pairs per B200, N B200 as replicas)"
+METRIC = "512^2 inpaints/sec (256 independent 512x512 image/mask pairs partitioned across N B200)"
 UNIT = "images/s"
 GFLOP_512 = 439.8  # algorithmic GFLOP of one 512^2 pass
 
@@ -160,13 +163,41 @@ def run_reference(args):
     v = statistics.mean(samples)
     cb["value"] = v
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "config 4: 512x512 image/mask pairs; reference arm runs the CPU engine "
                                    "restatement (Rust reference unbuildable offline) on a bounded sample"},
             "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        line.update(reference_cuda_timings())
     print(json.dumps(line), flush=True)
     return 0
+
+
+def reference_cuda_timings():
+    """The reference's CUDA path on this GPU, one image per pass as cuda::run
+    (lama-rs/src/cuda.rs:1542-1691) runs it: oracle/_ref/ref_cuda_bench
+    compiles the reference's lama-rs/cuda/lama.cu and replays cuda::run's
+    launch order (the five kernels of its absent toolkit are stand-ins: cuFFT
+    for the 2-D transforms).  Measurement only; absent when the harness was
+    not built or no GPU answers."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "ref_cuda_bench")
+    out = {}
+    if not os.path.exists(exe):
+        return {"ref_cuda": "unavailable: harness not built (no reference checkout where build() ran)"}
+    for side, passes, key in ((512, 10, "ref_cuda_ms_512_b1"), (1024, 5, "ref_cuda_ms_1024_b1")):
+        try:
+            r = subprocess.run([exe, str(side), str(passes), "2"], capture_output=True, text=True, timeout=600)
+            ms = None
+            for tok in r.stdout.split():
+                if tok.startswith("ms_per_pass="):
+                    ms = float(tok.split("=", 1)[1])
+            out[key] = ms if r.returncode == 0 and ms is not None else f"error: rc {r.returncode} {r.stderr[-200:]}"
+        except Exception as ex:  # reported, never required
+            out[key] = f"error: {ex}"
+    out["ref_cuda_note"] = ("reference lama.cu kernels replayed in cuda::run's launch order on this GPU, batch 1, "
+                            "CUDA events; lightgpu's absent FFT/elementwise kernels are stand-ins (cuFFT)")
+    return out
 
 
 def main():
@@ -215,22 +246,33 @@ def main():
     stream = torch.cuda.ExternalStream(eng.stream())
 
     from lama_b200.replicas import chunks as make_chunks, max_over_ranks, shard
-    mine = shard(IMAGES_PER_RANK * world, rank, world)
+    # config 4: the 256 images dealt round-robin over the ranks (strong scaling)
+    mine = shard(IMAGES_TOTAL, rank, world)
     n = len(mine)
     rgb_d, mask_d = make_data(N_DISTINCT, SIZE)
-    idx = np.array([i % N_DISTINCT for i in mine])
-    rgb_h = torch.from_numpy(rgb_d[idx]).pin_memory()
-    mask_h = torch.from_numpy(mask_d[idx]).pin_memory()
+    # the weak comparison gives every rank 256 images; the strong split is the
+    # first len(mine) of them on this rank (same pairs, same chunking rule)
+    n_weak = IMAGES_TOTAL if world > 1 else n
+    idx = np.array([i % N_DISTINCT for i in (mine if world == 1 else shard(IMAGES_TOTAL * world, rank, world))])
+    rgb_all = torch.from_numpy(rgb_d[idx]).cuda()
+    mask_all = torch.from_numpy(mask_d[idx]).cuda()
+    out_all = torch.empty_like(rgb_all)
+    rgb, mask, out = rgb_all[:n], mask_all[:n], out_all[:n]
+    rgb_h = rgb.cpu().pin_memory()
+    mask_h = mask.cpu().pin_memory()
     out_h = torch.empty_like(rgb_h).pin_memory()
-    rgb = rgb_h.cuda()
-    mask = mask_h.cuda()
-    out = torch.empty_like(rgb)
     chunks = make_chunks(n, args.chunk)
+    chunks_weak = make_chunks(n_weak, args.chunk)
     px = SIZE * SIZE
 
     def step_device():
         for s, c in chunks:
             eng.inpaint_u8_device(rgb[s].data_ptr(), mask[s].data_ptr(), out[s].data_ptr(), c, SIZE, SIZE)
+
+    def step_weak():
+        for s, c in chunks_weak:
+            eng.inpaint_u8_device(rgb_all[s].data_ptr(), mask_all[s].data_ptr(), out_all[s].data_ptr(), c, SIZE,
+                                  SIZE)
 
     def step_host():
         # lama_inpaint_u8_stream: the rank's images from pinned host memory in
@@ -273,8 +315,16 @@ def main():
     for _ in range(1):
         step_host()
     ms_e2e = timed(step_host, args.steps)
+    weak = None
+    if world > 1:
+        for _ in range(2):
+            step_weak()
+        ms_weak = timed(step_weak, args.steps)
+        weak = {"value": n_weak * world * args.steps / (ms_weak / 1e3), "unit": UNIT,
+                "images_per_rank": n_weak, "ms_per_step": ms_weak / args.steps,
+                "note": "every rank runs its own 256 images (replicas sharing nothing)"}
 
-    total = IMAGES_PER_RANK * world  # images all ranks process in one step
+    total = IMAGES_TOTAL  # images all ranks process in one step
     value = total * args.steps / (ms_dev / 1e3)
     e2e_value = total * args.steps / (ms_e2e / 1e3)
     # kernels per chunk: the u8 plan launches what the f32 plan does (its unfold
@@ -332,11 +382,15 @@ def main():
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_dev / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16x3 split on tensor cores)",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 I/O; convolutions as three bf16 tensor-core products of split operands (fp32 "
+                     "accumulation), activations stored as bf16 hi/lo pairs (16 significant bits); fp32 FFTs",
             "data": "synthetic: seeded value-noise images + brush masks (8 distinct pairs cycled), seeded BASELINE init",
-            "config": {"workload": "config 4: 256 x 512x512 pairs on each of N GPUs, weights replicated",
+            "config": {"workload": "config 4: 256 x 512x512 pairs partitioned round-robin over N GPUs, "
+                                   "weights replicated",
                        "images_per_rank": n, "chunk": args.chunk, "size": SIZE,
-                       "l2": "no flush needed: a 64-image chunk's activations are ~19 GB, inputs 256 MB > 126 MB L2",
+                       "l2": "no flush needed: a chunk's activations (~0.3 GB per image, >= 9.7 GB per chunk) "
+                             "exceed the 126 MB L2 many times over within every step",
                        "parallelism": f"replicas x{world}, no collectives"},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": total * px * 4, "d2h_bytes_per_step": total * px * 3,
@@ -345,6 +399,7 @@ def main():
             "roofline": roof,
             "cpu_baseline": cb,
             "clocks": clk,
+            "weak": weak,
             "gflop_per_image": GFLOP_512,
             "ms_per_1024_pass": extra.get("ms_per_1024_pass_b1"),
             "extra": extra,

@@ -135,6 +135,23 @@ void* lama_stream(lama_engine* e);
  * the shape exists; builds it if needed).  Returns < 0 on error. */
 int lama_launch_count(lama_engine* e, int batch, int h, int w);
 
+/* Capacity model (replaces mem.rs's estimated_bytes, lama-rs/src/mem.rs:13-36).
+ * Device bytes one inpaint pass of `batch` w x h images (lama_inpaint_u8,
+ * lama_inpaint_u8_device, one chunk of lama_inpaint_u8_stream; h and w are
+ * padded to multiples of 8) allocates on a B200, beyond the engine's resident
+ * weights (~0.2 GB): the pass's activations, spectral intermediates, split-K
+ * workspaces and u8 buffers, computed by building the pass's plan without
+ * allocating (no GPU or weight file needed).  Returns the byte count, or a
+ * negative LAMA_E* code for non-positive sizes.  Every plan is checked the
+ * same way before it allocates (mem.rs:49-73's guard, with its 10 % headroom
+ * of free memory): a pass that does not fit returns LAMA_ENOMEM with the
+ * needed and free amounts in lama_last_error(), before any allocation. */
+long long lama_estimate_bytes(int batch, int h, int w);
+
+/* The device bytes the engine's plan for that inpaint pass holds (building
+ * it if needed); equals lama_estimate_bytes on a B200. */
+int lama_plan_bytes(lama_engine* e, int batch, int h, int w, long long* bytes);
+
 /* Per-kernel-class timing of one forward pass on device buffers: each launch
  * is bracketed by CUDA events on the engine's stream.  Fills up to
  * `max_stats` records; *n_stats is the number of classes. */
@@ -212,9 +229,14 @@ int lama_section_rects(const uint8_t* mask, int w, int h, int* out, int cap);
  * loads the library, until exit) and calls no cudaMalloc / cudaFree.  The
  * first call on a device does that device's one-time set-up (it looks up the
  * array's device address and sets the kernels' shared-memory limit), so make
- * it before any stream capture on that device.
- *   d_feat: [batch][channels][h][w] fp32 (device);
- *   d_spec: [2][batch][h][w/2+1][2*channels] bf16 (device), value = part 0 +
+ * it before any stream capture on that device.  With CUDA's default lazy
+ * module loading the array's memory is claimed by that first call, not when
+ * the library is loaded: a caller that reserves the rest of the GPU for its
+ * own pool makes its first call before reserving it.  A failed set-up is not
+ * cached; the next call tries again.
+ *   d_feat: [batch][channels][h][w] fp32 (device, 4-byte aligned);
+ *   d_spec: [2][batch][h][w/2+1][2*channels] bf16 (device, 4-byte aligned;
+ *           a misaligned pointer returns LAMA_EINVAL), value = part 0 +
  *           part 1, channel 2c = real and 2c+1 = imaginary part of channel c
  *           (the engine's own spectrum layout).
  * Limits: h, w <= 1024 and batch*channels*(w/2+1)*h <= 2,097,152 (16 MiB of

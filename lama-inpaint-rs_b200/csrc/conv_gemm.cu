@@ -733,6 +733,9 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           if (lane == 0) {
             if (atomicAdd(split_cnt, 1) == 7) {
               *split_cnt = 0;
+              // the other seven warps' slices (each fenced before its count)
+              // are ordered before this part's arrival at the tile counter
+              __threadfence();
               last = atomicAdd(p.cnt + ti.split_tile, 1) == C.ksplit - 1;
               if (last) p.cnt[ti.split_tile] = 0;
               __threadfence_block();

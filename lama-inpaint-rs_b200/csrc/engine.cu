@@ -79,10 +79,20 @@ float bf2f(uint16_t h) {
 }
 
 // ------------------------------------------------------------------ device memory
+// A dry DevMem (capacity estimates) hands out distinct placeholder addresses
+// that are never dereferenced and only counts the bytes.
 struct DevMem {
   std::vector<void*> ptrs;
   size_t total = 0;
+  bool dry = false;
+  uintptr_t dry_next = (uintptr_t)1 << 40;
   void* alloc(size_t bytes, bool zero = true) {
+    if (dry) {
+      void* q = (void*)dry_next;
+      dry_next += (std::max<size_t>(bytes, 256) + 255) / 256 * 256;
+      total += bytes;
+      return q;
+    }
     void* p = nullptr;
     cudaError_t e = cudaMalloc(&p, std::max<size_t>(bytes, 256));
     if (e != cudaSuccess) {
@@ -118,6 +128,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// Set while a plan is built dry (capacity estimates): tensor maps are left
+// zero instead of being encoded, so no driver call is made.
+thread_local bool t_dry_build = false;
+
+CUresult encode_tiled(CUtensorMap* m, CUtensorMapDataType type, cuuint32_t rank, void* base, const cuuint64_t* dims,
+                      const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* estr,
+                      CUtensorMapInterleave il, CUtensorMapSwizzle sw, CUtensorMapL2promotion l2,
+                      CUtensorMapFloatOOBfill oob) {
+  if (t_dry_build) {
+    memset(m, 0, sizeof(*m));
+    return CUDA_SUCCESS;
+  }
+  return encode_fn()(m, type, rank, base, dims, strides, box, estr, il, sw, l2, oob);
+}
+
 // A split-bf16 NHWC activation: [2][B][H+2halo][W+2halo][C].
 struct Act {
   void* p = nullptr;
@@ -148,7 +173,7 @@ CUtensorMap act_map(const Act& a, int cb, int bw, int bh, int stride, bool inter
                            (cuuint64_t)a.part() * 2};
   cuuint32_t box[5] = {(cuuint32_t)cb, (cuuint32_t)(bw * stride), (cuuint32_t)(bh * stride), 1, (cuuint32_t)parts};
   cuuint32_t estr[5] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, base, dims, strides, box, estr,
+  CUresult r = encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, base, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE,
                            cb == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -173,7 +198,7 @@ CUtensorMap out_map(void* p, long long part, int B, int C, int H, int W, int hal
   const int bx = std::min(bw, 32);
   cuuint32_t box[5] = {32, (cuuint32_t)bx, (cuuint32_t)(32 / bx), 1, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, base, dims, strides, box, estr,
+  CUresult r = encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, base, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -198,7 +223,7 @@ CUtensorMap out_map_f32(void* p, bool nchw, int B, int C, int H, int W, int bw) 
     box[0] = 32; box[1] = (cuuint32_t)bx; box[2] = (cuuint32_t)(32 / bx); box[3] = 1;
   }
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p, dims, strides, box, estr,
+  CUresult r = encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE,
                            nchw ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -236,7 +261,7 @@ CUtensorMap w_map(const WClass& c, int bn, int parts = 1) {
   cuuint64_t strides[2] = {(cuuint64_t)c.k * 2, (cuuint64_t)c.npad * c.k * 2};
   cuuint32_t box[3] = {64, (cuuint32_t)bn, (cuuint32_t)parts};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c.w, dims, strides, box, estr,
+  CUresult r = encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c.w, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -479,6 +504,45 @@ void load_weights(const WeightFile& wf, Weights& W) {
   }
 }
 
+// The shapes (not the values) of every packed weight class, as load_weights
+// builds them: what a dry plan build needs to estimate a pass's memory
+// without a checkpoint or a GPU.
+void weight_shapes(Weights& W) {
+  auto cls = [](int n, int k) {
+    WClass c;
+    c.n = n;
+    c.k = k;
+    c.npad = (n + 15) / 16 * 16;
+    return c;
+  };
+  W.m1.cls = {cls(64, 256)};
+  W.m2.cls = {cls(128, 576)};
+  W.m3.cls = {cls(256, 1152)};
+  W.m4.cls = {cls(512, 2304)};
+  W.ffc.assign(36, FfcW());
+  for (FfcW& f : W.ffc) {
+    f.conv1.cls = {cls(192, 384)};
+    f.fu.cls = {cls(384, 384)};
+    f.out.cls = {cls(128, 4608), cls(384, 1344)};
+  }
+  const int ntaps[4] = {1, 2, 2, 4}, cins[3] = {512, 256, 128};
+  for (int u = 0; u < 3; u++) {
+    W.ct[u].cls.clear();
+    for (int ph = 0; ph < 4; ph++) W.ct[u].cls.push_back(cls(cins[u] / 2, ntaps[ph] * cins[u]));
+  }
+  W.outc.cls = {cls(160, 64)};
+}
+
+// The loaded checkpoint's packed classes have the shapes weight_shapes gives.
+void check_weight_shapes(Weights& loaded) {
+  Weights ref;
+  weight_shapes(ref);
+  std::vector<std::pair<int, int>> a, b;
+  for_each_gemm(loaded, [&](GemmW& g) { for (auto& c : g.cls) a.push_back({c.n, c.k}); });
+  for_each_gemm(ref, [&](GemmW& g) { for (auto& c : g.cls) b.push_back({c.n, c.k}); });
+  if (a != b) throw EngineError{LAMA_EUNSUPPORTED, "packed weight shapes differ from the capacity model"};
+}
+
 // ------------------------------------------------------------------ ops
 enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_IRFFT_PAR, OP_OUTCONV, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_TO_SPLIT, OP_TO_NCHW, OP_COPY };
 
@@ -590,6 +654,7 @@ struct Plan {
 struct lama_engine {
   int device = 0;
   int sms = 148;
+  std::string gpu_name = "the GPU";
   cudaStream_t stream = nullptr;
   std::string err;
   DevMem wmem;
@@ -899,7 +964,7 @@ struct Builder {
       t[k] = make_float2((float)std::cos(a), (float)std::sin(a));
     }
     float2* d = (float2*)pl.mem.alloc((size_t)n * sizeof(float2), false);
-    CK(cudaMemcpy(d, t.data(), (size_t)n * sizeof(float2), cudaMemcpyHostToDevice));
+    if (!pl.mem.dry) CK(cudaMemcpy(d, t.data(), (size_t)n * sizeof(float2), cudaMemcpyHostToDevice));
     return d;
   }
 
@@ -947,7 +1012,7 @@ struct Builder {
       cuuint64_t strides[1] = {256};
       cuuint32_t box[2] = {32, 256};
       cuuint32_t estr[2] = {1, 1};
-      CUresult r = encode_fn()(&feat_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, feat, dims, strides, box, estr,
+      CUresult r = encode_tiled(&feat_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, feat, dims, strides, box, estr,
                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
       if (r != CUDA_SUCCESS)
@@ -1103,12 +1168,9 @@ void check_device_error(lama_engine* e) {
   }
 }
 
-Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int nblocks) {
-  auto key = std::make_tuple(kind, B, H, W, h, w, nblocks);
-  auto it = e->plans.find(key);
-  if (it != e->plans.end()) return *it->second;
-  std::unique_ptr<Plan> pl(new Plan());
-  pl->kind = kind; pl->B = B; pl->H = H; pl->W = W; pl->h = h; pl->w = w; pl->nblocks = nblocks;
+// Every launch of a pass and the device memory it needs (all but the graph).
+void build_plan(lama_engine* e, Plan* pl) {
+  const int kind = pl->kind, B = pl->B, H = pl->H, W = pl->W, h = pl->h, w = pl->w, nblocks = pl->nblocks;
   Builder b{*e, *pl};
   if (kind == 0 || kind == 1 || kind == 3) {
     Act U = b.act(B, H + 6, W, 32, 0);
@@ -1180,6 +1242,50 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
       pl->ops.push_back(std::move(cv));
     }
   }
+}
+
+// Device bytes of a plan, from a dry build (the same code, no allocation).
+size_t plan_bytes_dry(lama_engine* e, int kind, int B, int H, int W, int h, int w, int nblocks) {
+  struct DryBuild {
+    DryBuild() { t_dry_build = true; }
+    ~DryBuild() { t_dry_build = false; }
+  } dry;
+  Plan pl;
+  pl.kind = kind; pl.B = B; pl.H = H; pl.W = W; pl.h = h; pl.w = w; pl.nblocks = nblocks;
+  pl.mem.dry = true;
+  build_plan(e, &pl);
+  return pl.mem.total;
+}
+
+std::string human_bytes(double b) {
+  char buf[32];
+  if (b >= (double)(1ull << 30)) snprintf(buf, sizeof(buf), "%.1f GB", b / (double)(1ull << 30));
+  else snprintf(buf, sizeof(buf), "%.0f MB", b / (double)(1ull << 20));
+  return buf;
+}
+
+Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int nblocks) {
+  auto key = std::make_tuple(kind, B, H, W, h, w, nblocks);
+  auto it = e->plans.find(key);
+  if (it != e->plans.end()) return *it->second;
+  // Capacity guard (lama-rs/src/mem.rs:49-73): refuse a pass the device
+  // cannot hold before anything is allocated, keeping the reference's 10 %
+  // headroom of free memory.  The estimate is the plan's exact footprint.
+  {
+    const size_t need = plan_bytes_dry(e, kind, B, H, W, h, w, nblocks);
+    size_t free_b = 0, total_b = 0;
+    CK(cudaMemGetInfo(&free_b, &total_b));
+    if (need > free_b - free_b / 10)
+      throw EngineError{LAMA_ENOMEM, "an inference over " + std::to_string(W) + "x" + std::to_string(H) +
+                                         (B > 1 ? " (batch " + std::to_string(B) + ")" : std::string()) +
+                                         " needs about " + human_bytes((double)need) +
+                                         " of device memory, but only " + human_bytes((double)free_b) +
+                                         " is free of " + human_bytes((double)total_b) + " on \"" + e->gpu_name +
+                                         "\""};
+  }
+  std::unique_ptr<Plan> pl(new Plan());
+  pl->kind = kind; pl->B = B; pl->H = H; pl->W = W; pl->h = h; pl->w = w; pl->nblocks = nblocks;
+  build_plan(e, pl.get());
   // Capture the pass into a CUDA graph.
   cudaGraph_t graph = nullptr;
   CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
@@ -1279,6 +1385,7 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
     std::string err;
     if (!wf.open(weights_path, err)) throw EngineError{LAMA_EWEIGHTS, err};
     load_weights(wf, e->W);
+    check_weight_shapes(e->W);
   } catch (const EngineError& x) {
     e->err = x.msg;
     return x.code;
@@ -1297,6 +1404,7 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
                                                prop.name + " sm_" + std::to_string(prop.major) +
                                                std::to_string(prop.minor)};
     e->sms = prop.multiProcessorCount;
+    e->gpu_name = prop.name;
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     CKL(conv_gemm_prepare());
     e->pair_clusters = conv_gemm_pair_clusters();
@@ -1548,6 +1656,37 @@ int lama_launch_count(lama_engine* e, int batch, int h, int w) {
     n = (int)get_plan(e, 0, batch, h, w, h, w, 18).ops.size();
   });
   return rc ? rc : n;
+}
+
+long long lama_estimate_bytes(int batch, int h, int w) {
+  if (batch < 1 || h < 1 || w < 1) return LAMA_EINVAL;
+  if ((long long)h * w > (1LL << 28) || batch > (1 << 16)) return LAMA_EINVAL;
+  try {
+    // a B200 as the engine sees it: 148 SMs, CTA-pair clusters available,
+    // automatic tiling and spectral paths
+    static lama_engine* shape_engine = [] {
+      lama_engine* x = new lama_engine();
+      weight_shapes(x->W);
+      x->sms = 148;
+      x->pair_clusters = 74;
+      return x;
+    }();
+    const int H = (h + 7) / 8 * 8, W = (w + 7) / 8 * 8;
+    return (long long)plan_bytes_dry(shape_engine, 1, batch, H, W, h, w, 18);
+  } catch (const EngineError& x) {
+    return x.code;
+  } catch (const std::exception&) {
+    return LAMA_EINVAL;
+  }
+}
+
+int lama_plan_bytes(lama_engine* e, int batch, int h, int w, long long* bytes) {
+  return guarded(e, [&] {
+    if (!bytes) throw EngineError{LAMA_EINVAL, "null buffer"};
+    check_shape(batch, h, w, false);
+    const int H = (h + 7) / 8 * 8, W = (w + 7) / 8 * 8;
+    *bytes = (long long)get_plan(e, 1, batch, H, W, h, w, 18).mem.total;
+  });
 }
 
 int lama_profile_forward(lama_engine* e, const float* d_in, int batch, int h, int w, float* d_out,

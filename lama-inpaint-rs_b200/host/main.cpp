@@ -162,9 +162,9 @@ struct Engine {
 
 // One window through the engine: build_input + forward + composite on the GPU.
 // `oom_hint` names the mode that caps the pass's size; it is added to the
-// message when the device refuses the pass's memory (mem.rs:48-73 refuses
-// such a pass before it starts; here the plan allocates everything before
-// any kernel runs, so the refusal is just as immediate).
+// message when the engine's capacity guard refuses the pass (as mem.rs:48-73
+// does, before anything is allocated: the engine compares the pass's exact
+// footprint with the device's free memory less 10 %).
 bool inpaint(Engine& eng, const Rgb8& src, const std::vector<uint8_t>& mask, Rgb8& out, std::string& err,
              const char* oom_hint) {
   out.width = src.width;

@@ -70,6 +70,9 @@ SIGNATURES = [
     ("lama_synchronize", ctypes.c_int, [_vp]),
     ("lama_stream", _vp, [_vp]),
     ("lama_launch_count", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    ("lama_estimate_bytes", ctypes.c_longlong, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    ("lama_plan_bytes", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       ctypes.POINTER(ctypes.c_longlong)]),
     ("lama_profile_forward", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp,
                                             ctypes.POINTER(KernelStat), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     ("lama_debug_run", ctypes.c_int, [_vp, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
@@ -110,6 +113,15 @@ def _up(a):
 
 
 # ------------------------------------------------------------ host geometry (no GPU)
+
+def estimate_bytes(batch: int, h: int, w: int) -> int:
+    """Device bytes one inpaint pass of `batch` w x h images allocates on a B200
+    (the capacity model behind the engine's guard; lama-rs/src/mem.rs:13-36)."""
+    v = lib().lama_estimate_bytes(batch, h, w)
+    if v < 0:
+        raise LamaError(int(v), "batch, h and w must be positive")
+    return int(v)
+
 
 def window_origin(c: int, side: int, extent: int) -> int:
     return lib().lama_window_origin(c, side, extent)
@@ -281,6 +293,12 @@ class Engine:
 
     def resblocks_device(self, d_l, d_g, d_lo, d_go, batch, h, w, nblocks=18):
         self._check(lib().lama_resblocks_device(self._h, d_l, d_g, batch, h, w, nblocks, d_lo, d_go))
+
+    def plan_bytes(self, batch: int, h: int, w: int) -> int:
+        """Device bytes the engine's inpaint plan for this shape holds (builds it)."""
+        v = ctypes.c_longlong(0)
+        self._check(lib().lama_plan_bytes(self._h, batch, h, w, ctypes.byref(v)))
+        return v.value
 
     def launch_count(self, batch: int, h: int, w: int) -> int:
         n = lib().lama_launch_count(self._h, batch, h, w)
