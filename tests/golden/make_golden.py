@@ -8,12 +8,20 @@ container_ref.safetensors
     repo's writer produces the same bytes from the same tensors and that both
     readers (the Python one and the engine's C++ one) parse it.
 
+ref_testdata_in.png, ref_testdata_mask.png
+    The reference's own example inputs (testdata/in.png, 512x512 RGB, and
+    testdata/mask.png, 512x512 grey, 38,000 masked pixels), copied byte for
+    byte; their SHA-256 digests are recorded in ref_testdata.json.  The GPU
+    tests run them through the CLI and compare with the oracle.
+
 Usage: python tests/golden/make_golden.py /path/to/reference
 """
 
+import hashlib
 import importlib.util
 import json
 import os
+import shutil
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -42,6 +50,14 @@ def main():
         json.dump({"writer": "lama-rs/safetensors_light.py:21-65", "tensors": N_TENSORS,
                    "seed": seeded.WEIGHT_SEED, "bytes": os.path.getsize(out)}, f, indent=1)
     print("wrote", out, os.path.getsize(out), "bytes")
+    digests = {}
+    for name in ("in.png", "mask.png"):
+        dst = os.path.join(HERE, "ref_testdata_" + name)
+        shutil.copyfile(os.path.join(ref, "testdata", name), dst)
+        digests["ref_testdata_" + name] = hashlib.sha256(open(dst, "rb").read()).hexdigest()
+    with open(os.path.join(HERE, "ref_testdata.json"), "w") as f:
+        json.dump({"source": "reference testdata/in.png and testdata/mask.png", "sha256": digests}, f, indent=1)
+    print("copied the reference's testdata PNGs")
 
 
 if __name__ == "__main__":

@@ -1,9 +1,12 @@
 """End-to-end CLI runs on the GPU: whole image, --tile, --sections, stdin/stdout.
 
-The whole-image and --tile outputs are checked against the oracle composite;
---sections is checked bit-for-bit against the same orchestration written in
-Python over the engine's u8 entry point (lama-rs/src/main.rs:465-566), so the
-test pins the CLI's section geometry, window crops and write-back.
+The whole-image and --tile outputs are checked against the oracle composite.
+The --sections tests here are consistency checks, not parity: the CLI and the
+device-resident driver (lama_inpaint_sections_u8) must give, bit for bit, the
+bytes of the reference's orchestration (lama-rs/src/main.rs:465-566) written
+in Python over the engine's per-window u8 entry point, which pins the section
+geometry, window crops and write-back.  Parity of --sections with the oracle
+is test_gpu_headline.py's.
 """
 
 import os

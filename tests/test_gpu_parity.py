@@ -292,10 +292,12 @@ def test_a_device_wait_that_runs_out_is_reported_and_the_engine_recovers(engine_
 
 
 def test_prefetching_rfft_matches_the_register_path_over_a_batch(engine_tamed):
-    """The persistent prefetching rfft2 (64x64 planes) walks several items per
-    CTA through its two TMA buffers once the batch has more than one item per
-    SM (4 images x 48 channel groups); the pass must match the register path."""
-    xs = np.stack([make_input(512, 512, s)[2] for s in (95, 96, 97, 98)])
+    """The persistent prefetching rfft2 (64x64 planes) runs min(items, 2 x 148)
+    CTAs; with 16 images x 48 channel groups = 768 items on 296 CTAs every CTA
+    walks two or three items through its TMA landing zone, prefetching the
+    next item's rows while it computes; the pass must match the register path."""
+    base = [make_input(512, 512, s)[2] for s in (95, 96, 97, 98)]
+    xs = np.stack([np.roll(base[i % 4], 29 * (i // 4), axis=2) for i in range(16)])
     try:
         engine_tamed.set_spectral_path(engine_tamed.SPECTRAL_REGISTER)
         ref = engine_tamed.forward(xs)
