@@ -5,17 +5,23 @@
 // complex values plus two twiddle tables.  Here they live in one file-scope
 // device array of fixed size, shared by every call in the process: nothing
 // in it has to start at zero (the intermediate is fully written by the row
-// pass before the column pass reads it, the tables are copied in by each
-// call), and calls whose GPU work overlaps in time - on different streams,
-// or from several host threads - race on it.  The entry point calls no
-// cudaMalloc, cudaFree or other allocating routine.  Host code cannot use the
-// array's name as a device pointer: the first call on each device, with that
-// device current, looks up its address (cudaGetSymbolAddress) and sets the
-// kernels' shared-memory limit; that first call belongs before any stream
-// capture on the device.
+// pass before the column pass reads it, and each call writes the twiddle
+// tables it reads with a small kernel first), and calls whose GPU work
+// overlaps in time - on different streams, or from several host threads -
+// race on it.  The entry point calls no cudaMalloc, cudaFree or other
+// allocating routine.  Host code cannot use the array's name as a device
+// pointer: the first call on each device, with that device current, looks up
+// its address (cudaGetSymbolAddress) and sets the kernels' shared-memory
+// limit; that first call belongs before any stream capture on the device.
+// With CUDA's lazy module loading (the default) the array's device memory is
+// claimed by that first look-up, not when the library is loaded, so a caller
+// that reserves the rest of the GPU for its own pool makes its first call
+// before reserving it.  A set-up that failed (for example for lack of memory)
+// is not remembered: the next call on that device tries again.
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdint>
 #include <mutex>
 
 #include "fft.cuh"
@@ -32,22 +38,46 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) float2 g_scratch[kScratchComplex + 2 * kMaxSide];
 
 struct DeviceSlot {
-  std::once_flag once;
-  cudaError_t status = cudaSuccess;
+  bool ready = false;
   float2* scratch = nullptr;
 };
 DeviceSlot g_slots[kMaxDevices];
+std::mutex g_setup_mutex;
 
-// Once per device, with that device current: the array's device address and
-// the kernels' shared-memory attribute.
+// Per device, with that device current, until it succeeds once: the array's
+// device address and the kernels' shared-memory attribute.
 cudaError_t setup(int device, float2** scratch) {
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
   DeviceSlot& s = g_slots[device];
-  std::call_once(s.once, [&s] {
-    s.status = cudaGetSymbolAddress((void**)&s.scratch, g_scratch);
-    if (s.status == cudaSuccess) s.status = (cudaError_t)fft_prepare(kSmem);
-  });
+  if (!s.ready) {
+    float2* p = nullptr;
+    cudaError_t st = cudaGetSymbolAddress((void**)&p, g_scratch);
+    if (st == cudaSuccess) st = (cudaError_t)fft_prepare(kSmem);
+    if (st != cudaSuccess) {
+      cudaGetLastError();  // clear the (non-sticky) error so the caller's next CUDA call does not report it
+      return st;
+    }
+    s.scratch = p;
+    s.ready = true;
+  }
   *scratch = s.scratch;
-  return s.status;
+  return cudaSuccess;
+}
+
+// Twiddle tables t[k] = (cos, sin)(2 pi k / n) of both plane sides, computed
+// in double and rounded to float (as the engine's host-built tables are).
+__global__ void k_noalloc_twiddles(float2* tw_h, int h, float2* tw_w, int w) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < h) {
+    double sn, cs;
+    sincospi(2.0 * (double)i / (double)h, &sn, &cs);
+    tw_h[i] = make_float2((float)cs, (float)sn);
+  }
+  if (i < w) {
+    double sn, cs;
+    sincospi(2.0 * (double)i / (double)w, &sn, &cs);
+    tw_w[i] = make_float2((float)cs, (float)sn);
+  }
 }
 
 int fail(char* err, int err_len, int code, const char* fmt, ...) {
@@ -67,13 +97,6 @@ int log2_or_neg(int n) {
   return l;
 }
 
-void fill_twiddles(float2* t, int n) {
-  for (int k = 0; k < n; k++) {
-    const double a = 2.0 * M_PI * (double)k / (double)n;
-    t[k] = make_float2((float)std::cos(a), (float)std::sin(a));
-  }
-}
-
 }  // namespace
 }  // namespace lama
 
@@ -85,6 +108,10 @@ extern "C" int lama_rfft2_noalloc(int device, const float* d_feat, int batch, in
   if (batch < 1 || channels < 1 || h < 1 || w < 1)
     return fail(err, err_len, LAMA_EINVAL, "batch, channels, h and w must be positive");
   if (channels > 65535) return fail(err, err_len, LAMA_EINVAL, "channels %d exceeds 65535", channels);
+  // the row pass reads feat as floats and the column pass stores the
+  // spectrum as pairs of bf16 (4-byte words)
+  if (((uintptr_t)d_feat & 3) || ((uintptr_t)d_spec & 3))
+    return fail(err, err_len, LAMA_EINVAL, "d_feat and d_spec must be 4-byte aligned");
   if (h > kMaxSide || w > kMaxSide)
     return fail(err, err_len, LAMA_ESCRATCH, "plane %dx%d exceeds the fixed scratch limit of %d per side", h, w,
                 kMaxSide);
@@ -122,19 +149,15 @@ extern "C" int lama_rfft2_noalloc(int device, const float* d_feat, int batch, in
     rc = fail(err, err_len, LAMA_ECUDA, "scratch set-up on device %d: %s", device, cudaGetErrorString(ce));
   } else {
     const cudaStream_t st = (cudaStream_t)stream;
-    float2 tw[2 * kMaxSide];
-    fill_twiddles(tw, h);
-    fill_twiddles(tw + kMaxSide, w);
     p.tmp = scratch;
     p.tw_h = scratch + kScratchComplex;
     p.tw_w = scratch + kScratchComplex + kMaxSide;
     p.feat = d_feat;
     p.spec = d_spec;
     p.spec_part = (long long)batch * h * wh * 2 * channels;
-    // pageable source: each copy returns once tw has been consumed
-    ce = cudaMemcpyAsync((void*)p.tw_h, tw, sizeof(float2) * (size_t)h, cudaMemcpyHostToDevice, st);
-    if (ce == cudaSuccess)
-      ce = cudaMemcpyAsync((void*)p.tw_w, tw + kMaxSide, sizeof(float2) * (size_t)w, cudaMemcpyHostToDevice, st);
+    const int n = h > w ? h : w;
+    k_noalloc_twiddles<<<(n + 255) / 256, 256, 0, st>>>((float2*)p.tw_h, h, (float2*)p.tw_w, w);
+    ce = cudaGetLastError();
     if (ce == cudaSuccess) ce = (cudaError_t)launch_rfft2(p, st);
     if (ce != cudaSuccess) rc = fail(err, err_len, LAMA_ECUDA, "rfft2 launch: %s", cudaGetErrorString(ce));
   }
