@@ -457,6 +457,17 @@ def extra_timings(eng, stream):
         except Exception as ex:
             out[key] = f"error: {ex}"
     try:
+        # per-op CUDA-event profile of the batch-1 512^2 pass (eager: one launch
+        # at a time on one stream, so the graph's second lane does not overlap here)
+        x = torch.rand((1, 4, 512, 512), device="cuda")
+        y = torch.empty((1, 3, 512, 512), device="cuda")
+        eng.profile_forward(x.data_ptr(), y.data_ptr(), 1, 512, 512)
+        st = eng.profile_forward(x.data_ptr(), y.data_ptr(), 1, 512, 512)
+        out["b1_512_ops"] = [{"name": s["name"], "launches": s["launches"], "ms": round(s["ms"], 4)} for s in st]
+        out["b1_512_eager_ms"] = sum(s["ms"] for s in st)
+    except Exception as ex:
+        out["b1_512_ops"] = f"error: {ex}"
+    try:
         l = torch.randn((1, 128, 64, 64), device="cuda")
         g = torch.randn((1, 384, 64, 64), device="cuda")
         lo, go = torch.empty_like(l), torch.empty_like(g)

@@ -102,7 +102,8 @@ int lama_resblocks_device(lama_engine* e, const float* d_local_in, const float* 
 
 /* Tile policy of the convolution GEMMs for plans built after this call
  * (cached plans are dropped): LAMA_TILING_AUTO uses pixel-major tiles,
- * shared by CTA pairs when a launch has at least two M tiles per SM,
+ * shared by CTA pairs when a launch has at least two M tiles per SM or when a
+ * small launch of 3x3-style taps can use the row union (with split K),
  * LAMA_TILING_SWAPPED uses channel-major tiles (M = 128 output channels,
  * N = 256 pixels) wherever they apply, LAMA_TILING_PIXEL uses single-CTA
  * pixel-major tiles only, LAMA_TILING_PAIRED uses pixel-major tiles shared by
@@ -121,6 +122,15 @@ int lama_set_tiling(lama_engine* e, int policy);
  * tests use this to cover each. */
 enum { LAMA_SPECTRAL_AUTO = 0, LAMA_SPECTRAL_TWO_PASS = 1, LAMA_SPECTRAL_REGISTER = 2, LAMA_SPECTRAL_PREFETCH = 3 };
 int lama_set_spectral_path(lama_engine* e, int path);
+
+/* Graph lanes of small-batch passes (no counterpart in the reference, which
+ * runs one launch at a time on the default stream).  Where an FFC layer's
+ * GEMM has fewer than two 128 x 128 output tiles per SM (e.g. a batch-1
+ * 512x512 pass), the layer's spectral chain (conv1, rfft2, FourierUnit conv,
+ * irfft2) runs on `chain_sms` SMs concurrently with the part of the FFC GEMM
+ * that does not need it, on the others.  0 = one lane; -1 = the default (40).
+ * Drops cached plans. */
+int lama_set_lanes(lama_engine* e, int chain_sms);
 
 /* Message of the last failure on this engine ("" if none). */
 const char* lama_last_error(const lama_engine* e);

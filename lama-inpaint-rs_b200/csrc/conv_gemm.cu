@@ -64,9 +64,9 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
 struct TileInfo {
   int cls, nt, b, i0, j0;
   bool dummy;      // CTA-pair tile past the class's last M tile (loads zeros, stores nothing)
-  int kb0, kb1;    // K blocks of this tile (a part of the class's K with split-K)
+  int kb0, kb1;    // K units of this tile (K blocks, or row-union iterations; a part of the class's K with split-K)
   int part;        // split-K part of this tile
-  int split_tile;  // split-K: workspace slice of part 0 of this output tile (slices part 0..ksplit-1 follow)
+  int split_tile;  // split-K: workspace slice of part 0 of this CTA's output tile (slices part 0..ksplit-1 follow)
 };
 
 // Tile t of the launch.  With CTA pairs (p.pair) t counts pair tiles: the
@@ -78,15 +78,15 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t, int 
   const GemmClass& C = p.cls[c];
   int lt = t - C.tile0;
   ti.cls = c;
-  const int part = lt % C.ksplit;  // split-K parts of one output tile are consecutive tiles
-  lt /= C.ksplit;
-  ti.kb0 = part * C.nkb / C.ksplit;
-  ti.kb1 = (part + 1) * C.nkb / C.ksplit;
+  const int part = C.part0 + lt % C.nparts;  // split-K parts of one output tile are consecutive tiles
+  lt /= C.nparts;
+  ti.kb0 = C.kcut[part];
+  ti.kb1 = C.kcut[part + 1];
   ti.part = part;
   ti.nt = lt % C.ntiles_n;
   int mt = lt / C.ntiles_n;
-  ti.split_tile = C.ws_tile0 + (mt * C.ntiles_n + ti.nt) * C.ksplit;
   if (p.pair) mt = 2 * mt + rank;
+  ti.split_tile = C.ws_tile0 + (mt * C.ntiles_n + ti.nt) * C.ksplit;
   ti.dummy = mt >= p.m_tiles;
   int per_img = p.tiles_y * p.tiles_x;
   ti.b = mt / per_img;
@@ -477,13 +477,15 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           const TileInfo ti = decode_tile(p, t, rank);
           const GemmClass& C = p.cls[ti.cls];
           const int wrow = ti.nt * BN + rank * BROWS;
-          for (int g = 0; g < C.ngroup && ok; g++) {
+          int u = 0;  // union iteration (group, block) in class order; this part runs [kb0, kb1)
+          for (int g = 0; g < C.ngroup && ok && u < ti.kb1; g++) {
             const GemmGroup& G = C.grp[g];
             const GemmSeg& S = C.seg[G.seg];
             const int tsh = p.cb == 32 ? 1 : 0;                          // log2(taps per K block)
             const uint32_t bytes = (uint32_t)p.urows[S.amap] * (uint32_t)p.bw * (uint32_t)p.cb * 4u +
                                    (uint32_t)(G.ndy >> tsh) * 2u * B_PART;
-            for (int blk = 0; blk < S.nblk; blk++) {
+            for (int blk = 0; blk < S.nblk && u < ti.kb1; blk++, u++) {
+              if (u < ti.kb0) continue;
               if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, 1)) { ok = false; break; }
               const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
               if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), PAIR ? 2 * bytes : bytes);
@@ -519,13 +521,15 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
           uint32_t accum = 0;
-          for (int g = 0; g < C.ngroup && ok; g++) {
+          int u = 0;  // as in the producer
+          for (int g = 0; g < C.ngroup && ok && u < ti.kb1; g++) {
             const GemmGroup& G = C.grp[g];
             const GemmSeg& S = C.seg[G.seg];
             const bool sw64 = p.cb == 32;
             const uint32_t rowb = (uint32_t)p.bw * (uint32_t)p.cb * 2u;     // one pixel row of the box
             const uint32_t apart = (uint32_t)p.urows[S.amap] * rowb;        // hi part of the box
-            for (int blk = 0; blk < S.nblk; blk++) {
+            for (int blk = 0; blk < S.nblk && u < ti.kb1; blk++, u++) {
+              if (u < ti.kb0) continue;
               if (!mbar_wait(full_bar(stage), phase, p.err, 3)) { ok = false; break; }
               tc_fence_after();
               const uint32_t sa = smem0 + (uint32_t)stage * 2u * STAGE;
@@ -709,9 +713,9 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       // split-K: every part stores its raw sums in its own workspace slice; the
       // CTA whose part arrives last finishes the tile from the sum of the
       // slices in part order (deterministic), the others are done
-      const bool split = (CH == 32 && !SWAP && !PAIR) && C.ksplit > 1;
+      const bool split = (CH == 32 && !SWAP) && C.ksplit > 1;
       const float* wsp = nullptr;
-      if constexpr (CH == 32 && !SWAP && !PAIR) {
+      if constexpr (CH == 32 && !SWAP) {
         if (split) {
           wsp = p.ws + (size_t)ti.split_tile * (BN * 128) + m;  // slice [n][m] of part 0
           float* mine = p.ws + (size_t)(ti.split_tile + ti.part) * (BN * 128) + m;
@@ -763,10 +767,23 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
         if (split) {
 #pragma unroll
           for (int k = 0; k < 32; k++) v[k] = __ldcg(wsp + (ch * 32 + k) * 128);
-          for (int q = 1; q < C.ksplit; q++) {
-            const float* sl = wsp + (size_t)q * (BN * 128);
+          // two slices' loads in flight at a time; the sum stays in part order
+#pragma unroll 1
+          for (int q = 1; q < C.ksplit; q += 2) {
+            const float* sa = wsp + (size_t)q * (BN * 128) + ch * 32 * 128;
+            const float* sb = sa + (BN * 128);
+            const bool two = q + 1 < C.ksplit;
+            float a[32], b[32];
 #pragma unroll
-            for (int k = 0; k < 32; k++) v[k] += __ldcg(sl + (ch * 32 + k) * 128);
+            for (int k = 0; k < 32; k++) a[k] = __ldcg(sa + k * 128);
+#pragma unroll
+            for (int k = 0; k < 32; k++) b[k] = two ? __ldcg(sb + k * 128) : 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; k++) v[k] += a[k];
+            if (two) {
+#pragma unroll
+              for (int k = 0; k < 32; k++) v[k] += b[k];
+            }
           }
         } else {
           tmem_ld32(trow + ch * 32, v);

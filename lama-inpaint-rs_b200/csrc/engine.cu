@@ -560,6 +560,17 @@ struct Op {
   UnfoldParams u{};
   ConvertParams cv{};
   double flops = 0, bytes = 0;
+  // split-K: workspace floats and tile counters this GEMM needs; ops of one
+  // lane run one after another, so they share the plan's workspace of that
+  // lane (the finisher of a tile resets its counter)
+  size_t ws_floats = 0;
+  int ws_counters = 0;
+  // Graph lanes: lane 1 ops run on a second stream concurrently with lane 0;
+  // `waits` are earlier ops of the other lane this op must follow (within a
+  // lane, program order).  Eager runs (profiling, debug) issue every op on
+  // one stream in plan order, which respects the same dependencies.
+  int lane = 0;
+  std::vector<int> waits;
   // output tensor, for the diagnostics entry points: split bf16 or fp32,
   // dims = (B, rows, cols, channels) of the stored layout (halo included;
   // NCHW outputs report (B, C, H, W)).
@@ -577,7 +588,7 @@ int launch_op(const Op& op, cudaStream_t st) {
     case OP_RFFT_REG: return launch_fft_reg(op.f, false, st);
     case OP_IRFFT_REG: return launch_fft_reg(op.f, true, st);
     case OP_RFFT_PF: return launch_rfft2_pf(*op.fpf, op.grid, st);
-    case OP_IRFFT_PAR: return launch_irfft2_par(op.f, st);
+    case OP_IRFFT_PAR: return launch_irfft2_par(op.f, op.grid, st);
     case OP_OUTCONV: return launch_outconv(*op.oc, op.grid, st);
     case OP_UNFOLD_F32: return launch_unfold_f32(op.u, st);
     case OP_UNFOLD_U8: return launch_unfold_u8(op.u, st);
@@ -635,6 +646,8 @@ void choose_tile(int mh, int mw, int& bh, int& bw, int px = 128, int stride = 1)
 }  // namespace
 
 // ------------------------------------------------------------------ engine
+constexpr int kDefaultChainSms = 40;
+
 struct Plan {
   int kind = 0;  // 0 f32 forward, 1 u8 inpaint, 2 resblocks, 3 one --sections pass (window)
   int B = 0, H = 0, W = 0, h = 0, w = 0, nblocks = 0;
@@ -656,6 +669,7 @@ struct lama_engine {
   int sms = 148;
   std::string gpu_name = "the GPU";
   cudaStream_t stream = nullptr;
+  cudaStream_t side_stream = nullptr;  // the second graph lane's stream during capture
   std::string err;
   DevMem wmem;
   Weights W;
@@ -663,6 +677,7 @@ struct lama_engine {
   int tiling = LAMA_TILING_AUTO;
   int spectral = LAMA_SPECTRAL_AUTO;
   int pair_clusters = 0;  // co-resident CTA-pair clusters (0: no pair tiles)
+  int chain_sms = kDefaultChainSms;  // SMs of the spectral graph lane at small batches (0: one lane)
   std::map<std::tuple<int, int, int, int, int, int, int>, std::unique_ptr<Plan>> plans;
   // lama_inpaint_u8_stream: copy stream and double-buffered staging
   cudaStream_t copy_stream = nullptr;
@@ -685,6 +700,19 @@ constexpr size_t kFftSmem = 160 * 1024;  // dynamic shared memory cap of the two
 struct Builder {
   lama_engine& e;
   Plan& pl;
+
+  void build_ops();  // every launch of the plan's pass, in order
+
+  // SMs of the spectral lane for an FFC stack of B images of h x w latents,
+  // or 0 for one lane: small launches (fewer than two 128 x 128 output tiles
+  // of the FFC GEMM per SM) whose latent suits the row-union CTA-pair tiles.
+  int lanes_for(int B, int h, int w) const {
+    if (e.chain_sms <= 0 || e.tiling != LAMA_TILING_AUTO || e.pair_clusters <= 0) return 0;
+    if (w % 32 || h % 4) return 0;
+    const long long outs = (long long)B * ((h * w + 127) / 128) * 4;
+    if (outs >= 2LL * e.sms) return 0;
+    return std::min(e.chain_sms, e.sms / 2);
+  }
 
   // The register-resident spectral kernels are the faster choice wherever
   // they apply (measured at batch 1 and 32 on 64x64 planes).
@@ -715,9 +743,16 @@ struct Builder {
     return fallback;
   }
 
+  // One GEMM launch (pushed to the plan).  max_sms caps the SMs it runs on
+  // (0 = all; graph lanes share the GPU); tail_class >= 0 runs that class's
+  // last K segment as its own split-K part in a second launch pushed right
+  // after the first (tail_flops of the algorithmic FLOPs), which finishes the
+  // class's tiles from the first launch's partial sums.
   void gemm(const std::string& name, const GemmW& Wt, const std::vector<AmapSpec>& amaps,
             const std::vector<ClassSpec>& classes, int cb, int B, int mh, int mw, const OutSpec& o, int relu,
-            int sigmoid, double flops) {
+            int sigmoid, double flops, int max_sms = 0, int tail_class = -1, double tail_flops = 0) {
+    const int sms = max_sms > 0 ? std::min(max_sms, e.sms) : e.sms;
+    const int clusters = std::min(e.pair_clusters, sms / 2);
     Op op;
     op.kind = OP_GEMM;
     op.name = name;
@@ -756,13 +791,33 @@ struct Builder {
     p.m_tiles = B * p.tiles_y * p.tiles_x;
     std::vector<int> ns;
     for (auto& c : classes) ns.push_back(c.nvalid);
-    const int bn = swap ? 256 : choose_bn(ns, p.m_tiles);
+    // Small launches (under two 128 x 128 output tiles per SM, e.g. the FFC
+    // layers of a batch-1 pass) whose taps allow the row union run as CTA
+    // pairs of 256 x 128 tiles with the union and split K: each SM then stages
+    // a quarter of the operand bytes per MMA that 128 x 64 tiles with per-tap
+    // boxes need, which is what bounds such launches (L2 -> SM traffic).
+    bool small_union = false;
+    if (!swap && e.tiling == LAMA_TILING_AUTO && cb == 64 && e.pair_clusters > 0 && mw % 32 == 0 && mh % 4 == 0) {
+      long long outs = 0;
+      bool ok = true, taps = false;
+      for (auto& c : classes) {
+        ok = ok && c.nvalid % 128 == 0;
+        outs += (long long)p.m_tiles * (c.nvalid / 128);
+        for (auto& sg : c.segs) {
+          ok = ok && sg.stride == 1;
+          taps = taps || sg.taps.size() > 1;
+        }
+      }
+      small_union = ok && taps && outs < 2LL * e.sms;
+    }
+    const int bn = swap ? 256 : small_union ? 128 : choose_bn(ns, p.m_tiles);
     if (!bn) throw EngineError{LAMA_EUNSUPPORTED, name + ": no tile width divides the output channels"};
     op.bn = bn;
     // CTA pairs (256 x BN tiles over two SMs) where the kernel has them and
-    // there are enough tiles for every SM
+    // there are enough tiles for every SM (or split K fills it, above)
     const bool pair = !swap && conv_gemm_pair_bn(bn) && e.pair_clusters > 0 &&
-                      (e.tiling == LAMA_TILING_PAIRED || (e.tiling == LAMA_TILING_AUTO && p.m_tiles >= 2 * e.sms));
+                      (e.tiling == LAMA_TILING_PAIRED || small_union ||
+                       (e.tiling == LAMA_TILING_AUTO && p.m_tiles >= 2 * e.sms));
     p.pair = pair ? 1 : 0;
     // Row union: 3x3-style taps that share dx read the row windows of one box
     // of bh + 2 rows per 64-channel block instead of one box per tap.  Tiles
@@ -856,24 +911,8 @@ struct Builder {
       if (C.nkb * 64 != wc.k)
         throw EngineError{LAMA_EUNSUPPORTED, name + ": K mismatch between plan and packed weights"};
     }
-    // Split-K for launches too small to fill the GPU (batch-1 passes): K parts
-    // of at most ~the per-SM share of all K blocks, finished in-kernel by the
-    // last part (pixel-major single-CTA tiles, 32-column chunks).
-    long long kbs = 0;
-    for (size_t ci = 0; ci < classes.size(); ci++) kbs += (long long)p.m_tiles * p.cls[ci].ntiles_n * p.cls[ci].nkb;
-    const int share = (int)std::max<long long>(12, (kbs + e.sms - 1) / e.sms);
-    const bool can_split = !swap && !pair && bn >= 32;
-    int ws_tiles = 0;
-    for (size_t ci = 0; ci < classes.size(); ci++) {
-      GemmClass& C = p.cls[ci];
-      C.ksplit = can_split ? std::min(8, std::max(1, (C.nkb + share - 1) / share)) : 1;
-      C.ksplit = std::min(C.ksplit, C.nkb);
-      C.ws_tile0 = ws_tiles;
-      if (C.ksplit > 1) ws_tiles += p.m_tiles * C.ntiles_n * C.ksplit;  // one slice per part
-      C.tile0 = tile0;
-      tile0 += (pair ? (p.m_tiles + 1) / 2 : p.m_tiles) * C.ntiles_n * C.ksplit;
-    }
-    if (uni && !ws_tiles) {
+    // Row-union groups of every class (kernel mode p.uni).
+    if (uni) {
       p.uni = 1;
       int span[GEMM_MAX_AMAPS] = {1, 1, 1};
       for (size_t ci = 0; ci < classes.size(); ci++) {
@@ -890,9 +929,79 @@ struct Builder {
         p.amap_u[i] = act_map(amaps[i].act, cb, bw, p.urows[i], 1, amaps[i].interior, 2);
       }
     }
-    if (ws_tiles) {
-      p.ws = (float*)pl.mem.alloc((size_t)ws_tiles * bn * 128 * sizeof(float), false);
-      p.cnt = (int*)pl.mem.alloc((size_t)ws_tiles * sizeof(int));  // zeroed; reset by each tile's finisher
+    // K units of each class and their weight in 64-wide K blocks: K blocks,
+    // or (row union) one unit per group and channel block, in group order.
+    std::vector<std::vector<int>> unit_kb(classes.size());
+    for (size_t ci = 0; ci < classes.size(); ci++) {
+      const GemmClass& C = p.cls[ci];
+      if (uni) {
+        for (int g = 0; g < C.ngroup; g++)
+          for (int blk = 0; blk < C.seg[C.grp[g].seg].nblk; blk++)
+            unit_kb[ci].push_back(cb == 32 ? C.grp[g].ndy / 2 : C.grp[g].ndy);
+      } else {
+        unit_kb[ci].assign(C.nkb, 1);
+      }
+    }
+    // Split-K for launches too small to fill the GPU (batch-1 passes): K parts
+    // of at most ~the per-SM (per-pair) share of all K blocks, finished
+    // in-kernel by the last part (32-column chunks).  Parts are cut at unit
+    // boundaries with balanced K blocks.
+    // (from the SM count alone, so that the plan's memory does not depend on
+    // how many clusters the device co-schedules)
+    const int slots = pair ? sms / 2 : sms;
+    const long long mt_sched = pair ? (p.m_tiles + 1) / 2 : p.m_tiles;  // output tiles per N tile as scheduled
+    long long kbs = 0;
+    for (size_t ci = 0; ci < classes.size(); ci++) kbs += mt_sched * p.cls[ci].ntiles_n * p.cls[ci].nkb;
+    const int share = pair ? (int)std::max<long long>(12, (kbs + 2 * slots - 1) / (2 * slots))
+                           : (int)std::max<long long>(12, (kbs + slots - 1) / slots);
+    const bool can_split = !swap && bn >= 32;
+    if (tail_class >= 0 && (!can_split || tail_class >= (int)classes.size() || classes[tail_class].segs.size() < 2))
+      throw EngineError{LAMA_EUNSUPPORTED, name + ": a separate tail launch needs a splittable class of two segments"};
+    int ws_tiles = 0;
+    for (size_t ci = 0; ci < classes.size(); ci++) {
+      GemmClass& C = p.cls[ci];
+      const std::vector<int>& uk = unit_kb[ci];
+      const bool tail = (int)ci == tail_class;
+      // units [0, nhead) are split into parts; a tail class's last segment
+      // (units [nhead, nunits)) is one more part of its own
+      const int nunits = (int)uk.size();
+      int nhead = nunits;
+      if (tail) {
+        nhead = 0;
+        const int last = C.nseg - 1;
+        if (uni) {
+          for (int g = 0; g < C.ngroup; g++)
+            if (C.grp[g].seg != last) nhead += C.seg[C.grp[g].seg].nblk;
+        } else {
+          nhead = C.seg[last].sub0 * cb / 64;
+        }
+      }
+      int kb_head = 0;
+      for (int u = 0; u < nhead; u++) kb_head += uk[u];
+      int nsplit = can_split ? std::min(GEMM_MAX_KSPLIT - (tail ? 1 : 0), std::max(1, (kb_head + share - 1) / share)) : 1;
+      nsplit = std::min(nsplit, nhead);
+      // cut q ends at the first unit boundary with >= (q + 1) / nsplit of the head's K blocks
+      C.kcut[0] = 0;
+      int u = 0, acc = 0;
+      for (int q = 0; q < nsplit; q++) {
+        const long long goal = (long long)kb_head * (q + 1) / nsplit;
+        while (u < nhead && (acc < goal || u <= C.kcut[q]) && nhead - u > nsplit - 1 - q) acc += uk[u++];
+        C.kcut[q + 1] = (int16_t)u;
+      }
+      C.kcut[nsplit] = (int16_t)nhead;
+      C.ksplit = nsplit;
+      if (tail) C.kcut[++C.ksplit] = (int16_t)nunits;
+      C.part0 = 0;
+      C.nparts = tail ? C.ksplit - 1 : C.ksplit;
+      C.ws_tile0 = ws_tiles;
+      // one slice per part and per CTA-sized output tile (pairs: per CTA of the pair)
+      if (C.ksplit > 1) ws_tiles += (int)(pair ? 2 * mt_sched : p.m_tiles) * C.ntiles_n * C.ksplit;
+      C.tile0 = tile0;
+      tile0 += (int)mt_sched * C.ntiles_n * C.nparts;
+    }
+    if (ws_tiles) {  // pointers are set once the plan's shared workspace exists
+      op.ws_floats = (size_t)ws_tiles * bn * 128;
+      op.ws_counters = ws_tiles;
     }
     p.total_tiles = tile0;
     p.scale = Wt.scale;
@@ -934,7 +1043,7 @@ struct Builder {
       }
       p.obox_w = std::min(bw, 32);
     }
-    op.grid = pair ? 2 * std::min(p.total_tiles, e.pair_clusters) : std::min(p.total_tiles, e.sms);
+    op.grid = pair ? 2 * std::min(p.total_tiles, clusters) : std::min(p.total_tiles, sms);
     op.out_ptr = o.p;
     op.out_split = o.kind == OUT_SPLIT;
     op.out_part = o.part;
@@ -943,7 +1052,36 @@ struct Builder {
     } else {
       op.dims[0] = B; op.dims[1] = o.h + 2 * o.halo; op.dims[2] = o.w + 2 * o.halo; op.dims[3] = o.c;
     }
+    if (tail_class < 0) {
+      pl.ops.push_back(std::move(op));
+      return;
+    }
+    // the tail launch: the tail class alone, its last part, same workspace slices
+    Op tl;
+    tl.kind = OP_GEMM;
+    tl.name = name;
+    tl.bn = op.bn;
+    tl.flops = tail_flops;
+    op.flops -= tail_flops;
+    tl.g.reset(new GemmParams(p));
+    GemmParams& q = *tl.g;
+    q.nclass = 1;
+    q.cls[0] = p.cls[tail_class];
+    q.cls[0].part0 = q.cls[0].ksplit - 1;
+    q.cls[0].nparts = 1;
+    q.cls[0].tile0 = 0;
+    q.bmap[0] = p.bmap[tail_class];
+    q.omap[0] = p.omap[tail_class];
+    q.total_tiles = (int)mt_sched * q.cls[0].ntiles_n;
+    tl.grid = pair ? 2 * std::min(q.total_tiles, clusters) : std::min(q.total_tiles, sms);
+    tl.ws_floats = op.ws_floats;
+    tl.ws_counters = op.ws_counters;
+    tl.out_ptr = op.out_ptr;
+    tl.out_split = op.out_split;
+    tl.out_part = op.out_part;
+    for (int i = 0; i < 4; i++) tl.dims[i] = op.dims[i];
     pl.ops.push_back(std::move(op));
+    pl.ops.push_back(std::move(tl));
   }
 
   static OutSpec split_out(const Act& a, const void* skip = nullptr) {
@@ -1019,38 +1157,56 @@ struct Builder {
         throw EngineError{LAMA_ECUDA, "cuTensorMapEncodeTiled (feat rows) failed: " + std::to_string((int)r)};
     }
     const double px = (double)B * h * w, pxs = (double)B * h * wh;
+    // Small batches run each FFC layer on two graph lanes: the spectral chain
+    // (conv1, rfft2, FourierUnit conv, irfft2: short launches of a few dozen
+    // CTAs each) on `chain` SMs, concurrently with the part of the FFC GEMM
+    // that does not need its result (the local class, and the l2g segment of
+    // the global class as split-K parts) on the other SMs; a tail launch then
+    // adds the conv2 segment over S and finishes the global class.
+    const int chain = lanes_for(B, h, w);
+    int prev0 = (int)pl.ops.size() - 1;  // last lane-0 op before the stack
+    auto on_lane1 = [&](int wait_for) {
+      if (!chain) return;
+      pl.ops.back().lane = 1;
+      if (wait_for >= 0) pl.ops.back().waits.push_back(wait_for);
+    };
     for (int blk = 0; blk < nblocks; blk++)
       for (int sub = 0; sub < 2; sub++) {
         const FfcW& F = e.W.ffc[(size_t)blk * 2 + sub];
         const Act& Xin = sub == 0 ? XA : XB;
         const Act& Xout = sub == 0 ? XB : XA;
-        const std::string tag = "b" + std::to_string(blk) + "." + std::to_string(sub + 1);
         // conv1 1x1 384 -> 192 on the global channels, BN, ReLU -> feat (fp32)
         gemm("spectral_conv1", F.conv1, {{Xin, 1, false}}, {one_seg(0, 0, 192, SegSpec{0, 128, 384, 1, {{1, 1}}})}, 64, B, h, w,
-             OutSpec{OUT_F32_NCHW, feat, 0, 192, h, w, 0, 0, nullptr}, 1, 0, 2.0 * px * 192 * 384);
+             OutSpec{OUT_F32_NCHW, feat, 0, 192, h, w, 0, 0, nullptr}, 1, 0, 2.0 * px * 192 * 384, chain);
+        on_lane1(prev0);
         Op r;
         r.kind = pf ? OP_RFFT_PF : reg ? OP_RFFT_REG : OP_RFFT;
         r.name = "rfft2";
         r.f = fp;
         if (pf) {
           r.fpf.reset(new FftPfParams{feat_map, fp});
-          r.grid = std::min(B * 192 / 4, 2 * e.sms);  // two CTAs per SM
+          r.grid = std::min(B * 192 / 4, 2 * (chain ? chain : e.sms));  // two CTAs per SM
         }
         r.bytes = px * 192 * 4 + pxs * 384 * 4;
         r.out_ptr = spec.p; r.out_split = 1; r.out_part = spec.part();
         r.dims[0] = B; r.dims[1] = h; r.dims[2] = wh; r.dims[3] = 384;
         pl.ops.push_back(std::move(r));
+        on_lane1(-1);
         // FourierUnit 1x1 384 -> 384 on the stacked spectrum, BN, ReLU -> fu (fp32)
         gemm("fourier_conv", F.fu, {{spec, 1, false}}, {one_seg(0, 0, 384, SegSpec{0, 0, 384, 1, {{0, 0}}})}, 64, B, 1, h * wh,
-             OutSpec{OUT_F32_NHWC, fu, 0, 384, 1, h * wh, 0, 0, nullptr}, 1, 0, 2.0 * pxs * 384 * 384);
+             OutSpec{OUT_F32_NHWC, fu, 0, 384, 1, h * wh, 0, 0, nullptr}, 1, 0, 2.0 * pxs * 384 * 384, chain);
+        on_lane1(-1);
         Op ir;
         ir.kind = pf ? OP_IRFFT_PAR : reg ? OP_IRFFT_REG : OP_IRFFT;
         ir.name = "irfft2";
         ir.f = fp;
+        ir.grid = e.sms;  // OP_IRFFT_PAR: picks its channels per CTA from the SM count
         ir.bytes = pxs * 384 * 4 + px * 192 * 4 + px * 192 * 4;
         ir.out_ptr = S.p; ir.out_split = 1; ir.out_part = S.part();
         ir.dims[0] = B; ir.dims[1] = h; ir.dims[2] = w; ir.dims[3] = 192;
         pl.ops.push_back(std::move(ir));
+        on_lane1(-1);
+        const int i_irfft = (int)pl.ops.size() - 1;
         // FFC outputs: local = 3x3 over [x_l | x_g]; global = 3x3 over x_l + 1x1 over S
         ClassSpec cl{0, 0, 128};
         cl.segs.push_back({0, 0, 512, 1, square_taps(3, 0)});
@@ -1058,7 +1214,10 @@ struct Builder {
         cgl.segs.push_back({0, 0, 128, 1, square_taps(3, 0)});
         cgl.segs.push_back({1, 0, 192, 1, {{0, 0}}});
         gemm("ffc_out", F.out, {{Xin, 1, false}, {S, 1, false}}, {cl, cgl}, 64, B, h, w,
-             split_out(Xout, sub == 1 ? XA.p : nullptr), 1, 0, 2.0 * px * (128.0 * 4608 + 384.0 * 1344));
+             split_out(Xout, sub == 1 ? XA.p : nullptr), 1, 0, 2.0 * px * (128.0 * 4608 + 384.0 * 1344),
+             chain ? e.sms - chain : 0, chain ? 1 : -1, 2.0 * px * 384.0 * 192);
+        if (chain) pl.ops.back().waits.push_back(i_irfft);  // the tail launch reads S
+        prev0 = (int)pl.ops.size() - 1;
       }
   }
 
@@ -1159,6 +1318,16 @@ struct Builder {
   }
 };
 
+// Events destroyed on every exit path, the error ones included.
+struct EventSet {
+  std::vector<cudaEvent_t> ev;
+  explicit EventSet(size_t n) : ev(n, nullptr) {}
+  ~EventSet() {
+    for (cudaEvent_t x : ev)
+      if (x) cudaEventDestroy(x);
+  }
+};
+
 void check_device_error(lama_engine* e) {
   int v = 0;
   CK(cudaMemcpy(&v, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -1170,11 +1339,34 @@ void check_device_error(lama_engine* e) {
 
 // Every launch of a pass and the device memory it needs (all but the graph).
 void build_plan(lama_engine* e, Plan* pl) {
-  const int kind = pl->kind, B = pl->B, H = pl->H, W = pl->W, h = pl->h, w = pl->w, nblocks = pl->nblocks;
   Builder b{*e, *pl};
+  b.build_ops();
+  // one split-K workspace per lane, sized for its largest GEMM
+  size_t wsf[2] = {0, 0};
+  int wsc[2] = {0, 0};
+  for (const Op& op : pl->ops) {
+    wsf[op.lane] = std::max(wsf[op.lane], op.ws_floats);
+    wsc[op.lane] = std::max(wsc[op.lane], op.ws_counters);
+  }
+  for (int l = 0; l < 2; l++) {
+    if (!wsc[l]) continue;
+    float* ws = (float*)pl->mem.alloc(wsf[l] * sizeof(float), false);
+    int* cnt = (int*)pl->mem.alloc((size_t)wsc[l] * sizeof(int));  // zeroed; reset by each tile's finisher
+    for (Op& op : pl->ops)
+      if (op.kind == OP_GEMM && op.lane == l && op.ws_counters) {
+        op.g->ws = ws;
+        op.g->cnt = cnt;
+      }
+  }
+}
+
+void Builder::build_ops() {
+  const int kind = pl.kind, B = pl.B, H = pl.H, W = pl.W, h = pl.h, w = pl.w, nblocks = pl.nblocks;
+  Plan* const pl_ = &pl;
+  Builder& b = *this;
   if (kind == 0 || kind == 1 || kind == 3) {
     Act U = b.act(B, H + 6, W, 32, 0);
-    if (kind == 0) pl->out = (float*)pl->mem.alloc((size_t)B * 3 * H * W * 4);
+    if (kind == 0) pl_->out = (float*)pl_->mem.alloc((size_t)B * 3 * H * W * 4);
     Op un;
     un.name = "unfold_input";
     un.u.batch = B; un.u.H = H; un.u.W = W; un.u.h = h; un.u.w = w;
@@ -1183,54 +1375,54 @@ void build_plan(lama_engine* e, Plan* pl) {
     un.out_ptr = U.p; un.out_split = 1; un.out_part = U.part();
     un.dims[0] = B; un.dims[1] = H + 6; un.dims[2] = W; un.dims[3] = 32;
     if (kind == 0) {
-      pl->in_f32 = (float*)pl->mem.alloc((size_t)B * 4 * H * W * 4);
+      pl_->in_f32 = (float*)pl_->mem.alloc((size_t)B * 4 * H * W * 4);
       un.kind = OP_UNFOLD_F32;
-      un.u.in = pl->in_f32;
+      un.u.in = pl_->in_f32;
     } else if (kind == 3) {
-      pl->win = (WinDesc*)pl->mem.alloc(sizeof(WinDesc));
+      pl_->win = (WinDesc*)pl_->mem.alloc(sizeof(WinDesc));
       un.kind = OP_UNFOLD_U8;
-      un.u.win = pl->win;
+      un.u.win = pl_->win;
     } else {
-      pl->rgb = (uint8_t*)pl->mem.alloc((size_t)B * h * w * 3);
-      pl->mask = (uint8_t*)pl->mem.alloc((size_t)B * h * w);
-      pl->out_rgb = (uint8_t*)pl->mem.alloc((size_t)B * h * w * 3);
+      pl_->rgb = (uint8_t*)pl_->mem.alloc((size_t)B * h * w * 3);
+      pl_->mask = (uint8_t*)pl_->mem.alloc((size_t)B * h * w);
+      pl_->out_rgb = (uint8_t*)pl_->mem.alloc((size_t)B * h * w * 3);
       un.kind = OP_UNFOLD_U8;
-      un.u.rgb = pl->rgb;
-      un.u.mask = pl->mask;
+      un.u.rgb = pl_->rgb;
+      un.u.mask = pl_->mask;
     }
-    pl->ops.push_back(std::move(un));
+    pl_->ops.push_back(std::move(un));
     if (kind == 1) {
       // the composite's unmasked bytes are the source bytes: copied whole
       // here, and the OutConv writes only the masked pixels
       Op cp;
       cp.kind = OP_COPY;
       cp.name = "copy_source";
-      cp.csrc = pl->rgb;
-      cp.cdst = pl->out_rgb;
+      cp.csrc = pl_->rgb;
+      cp.cdst = pl_->out_rgb;
       cp.cbytes = (size_t)B * h * w * 3;
-      pl->ops.push_back(std::move(cp));
-      const CompositeParams comp{B, h, w, H, W, pl->rgb, pl->mask, pl->out_rgb};
+      pl_->ops.push_back(std::move(cp));
+      const CompositeParams comp{B, h, w, H, W, pl_->rgb, pl_->mask, pl_->out_rgb};
       b.core(U, B, H, W, nullptr, &comp);
     } else if (kind == 3) {
       const CompositeParams comp{B, h, w, H, W, nullptr, nullptr, nullptr};
-      b.core(U, B, H, W, nullptr, &comp, pl->win);
+      b.core(U, B, H, W, nullptr, &comp, pl_->win);
     } else {
-      b.core(U, B, H, W, pl->out);
+      b.core(U, B, H, W, pl_->out);
     }
   } else {
     Act XA = b.act(B, H, W, 512, 1);
     Act XB = b.act(B, H, W, 512, 1);
-    pl->l_in = (float*)pl->mem.alloc((size_t)B * 128 * H * W * 4);
-    pl->g_in = (float*)pl->mem.alloc((size_t)B * 384 * H * W * 4);
-    pl->l_out = (float*)pl->mem.alloc((size_t)B * 128 * H * W * 4);
-    pl->g_out = (float*)pl->mem.alloc((size_t)B * 384 * H * W * 4);
+    pl_->l_in = (float*)pl_->mem.alloc((size_t)B * 128 * H * W * 4);
+    pl_->g_in = (float*)pl_->mem.alloc((size_t)B * 384 * H * W * 4);
+    pl_->l_out = (float*)pl_->mem.alloc((size_t)B * 128 * H * W * 4);
+    pl_->g_out = (float*)pl_->mem.alloc((size_t)B * 384 * H * W * 4);
     for (int i = 0; i < 2; i++) {
       Op cv;
       cv.kind = OP_TO_SPLIT;
       cv.name = "nchw_to_split";
-      cv.cv = ConvertParams{B, i == 0 ? 128 : 384, H, W, 1, 512, i == 0 ? 0 : 128, i == 0 ? pl->l_in : pl->g_in,
+      cv.cv = ConvertParams{B, i == 0 ? 128 : 384, H, W, 1, 512, i == 0 ? 0 : 128, i == 0 ? pl_->l_in : pl_->g_in,
                             XA.p, XA.part()};
-      pl->ops.push_back(std::move(cv));
+      pl_->ops.push_back(std::move(cv));
     }
     b.resblocks(XA, XB, nblocks);
     for (int i = 0; i < 2; i++) {
@@ -1238,8 +1430,8 @@ void build_plan(lama_engine* e, Plan* pl) {
       cv.kind = OP_TO_NCHW;
       cv.name = "split_to_nchw";
       cv.cv = ConvertParams{B, i == 0 ? 128 : 384, H, W, 1, 512, i == 0 ? 0 : 128,
-                            i == 0 ? pl->l_out : pl->g_out, XA.p, XA.part()};
-      pl->ops.push_back(std::move(cv));
+                            i == 0 ? pl_->l_out : pl_->g_out, XA.p, XA.part()};
+      pl_->ops.push_back(std::move(cv));
     }
   }
 }
@@ -1286,13 +1478,35 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
   std::unique_ptr<Plan> pl(new Plan());
   pl->kind = kind; pl->B = B; pl->H = H; pl->W = W; pl->h = h; pl->w = w; pl->nblocks = nblocks;
   build_plan(e, pl.get());
-  // Capture the pass into a CUDA graph.
+  // Capture the pass into a CUDA graph: lane 1 forks off the engine stream
+  // at its first op and joins back after its last, cross-lane waits become
+  // graph edges through events.
   cudaGraph_t graph = nullptr;
+  bool two_lanes = false;
+  for (const Op& op : pl->ops) two_lanes = two_lanes || op.lane == 1;
+  EventSet done(two_lanes ? pl->ops.size() + 1 : 0);
+  for (auto& x : done.ev) CK(cudaEventCreateWithFlags(&x, cudaEventDisableTiming));
+  std::vector<char> waited(pl->ops.size(), 0);
+  for (const Op& op : pl->ops)
+    for (int j : op.waits) waited[(size_t)j] = 1;
   CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
   int lerr = 0;
-  for (const Op& op : pl->ops) {
-    lerr = launch_op(op, e->stream);
-    if (lerr) break;
+  const cudaStream_t lane_stream[2] = {e->stream, e->side_stream};
+  if (two_lanes) {  // the side stream joins the capture from the engine stream
+    lerr = (int)cudaEventRecord(done.ev.back(), e->stream);
+    if (!lerr) lerr = (int)cudaStreamWaitEvent(e->side_stream, done.ev.back(), 0);
+  }
+  for (size_t i = 0; i < pl->ops.size() && !lerr; i++) {
+    const Op& op = pl->ops[i];
+    const cudaStream_t st = lane_stream[two_lanes ? op.lane : 0];
+    for (int j : op.waits)
+      if (!lerr && two_lanes) lerr = (int)cudaStreamWaitEvent(st, done.ev[(size_t)j], 0);
+    if (!lerr) lerr = launch_op(op, st);
+    if (!lerr && two_lanes && waited[i]) lerr = (int)cudaEventRecord(done.ev[i], st);
+  }
+  if (two_lanes && !lerr) {  // join: the engine stream waits for the side stream's last op
+    lerr = (int)cudaEventRecord(done.ev.back(), e->side_stream);
+    if (!lerr) lerr = (int)cudaStreamWaitEvent(e->stream, done.ev.back(), 0);
   }
   cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
   if (lerr) {
@@ -1354,16 +1568,6 @@ int launch_named(const Op& op, cudaStream_t st) {
   return r;
 }
 
-// Events destroyed on every exit path, the error ones included.
-struct EventSet {
-  std::vector<cudaEvent_t> ev;
-  explicit EventSet(size_t n) : ev(n, nullptr) {}
-  ~EventSet() {
-    for (cudaEvent_t x : ev)
-      if (x) cudaEventDestroy(x);
-  }
-};
-
 }  // namespace
 
 extern "C" {
@@ -1406,6 +1610,7 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
     e->sms = prop.multiProcessorCount;
     e->gpu_name = prop.name;
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&e->side_stream, cudaStreamNonBlocking));
     CKL(conv_gemm_prepare());
     e->pair_clusters = conv_gemm_pair_clusters();
     CKL(fft_prepare(kFftSmem));
@@ -1632,6 +1837,15 @@ int lama_set_tiling(lama_engine* e, int policy) {
   });
 }
 
+int lama_set_lanes(lama_engine* e, int chain_sms) {
+  return guarded(e, [&] {
+    if (chain_sms < -1 || chain_sms > e->sms / 2) throw EngineError{LAMA_EINVAL, "chain_sms must be in -1..sms/2"};
+    CK(cudaStreamSynchronize(e->stream));
+    e->plans.clear();
+    e->chain_sms = chain_sms < 0 ? kDefaultChainSms : chain_sms;
+  });
+}
+
 int lama_set_spectral_path(lama_engine* e, int path) {
   return guarded(e, [&] {
     if (path < LAMA_SPECTRAL_AUTO || path > LAMA_SPECTRAL_PREFETCH) throw EngineError{LAMA_EINVAL, "unknown spectral path"};
@@ -1812,6 +2026,7 @@ void lama_close(lama_engine* e) {
   }
   if (e->copy_stream) cudaStreamDestroy(e->copy_stream);
   e->wmem.free_all();
+  if (e->side_stream) cudaStreamDestroy(e->side_stream);
   if (e->stream) cudaStreamDestroy(e->stream);
   cudaGetLastError();
   delete e;

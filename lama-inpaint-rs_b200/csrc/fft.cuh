@@ -87,9 +87,11 @@ bool fft_reg_supported(int h, int w);
 bool fft_pf_supported(int c, int h, int w);
 int fft_pf_prepare();
 int launch_rfft2_pf(const FftPfParams& q, int grid, cudaStream_t st);
-// irfft2 of 64 x 64 planes split by output-row parity, 16 channels per CTA
-// (fft_reg.cu); needs c % 16 == 0.
-int launch_irfft2_par(const FftParams& p, cudaStream_t st);
+// irfft2 of 64 x 64 planes split by output-row parity, 16 channels per CTA,
+// or 4 where 16-channel CTAs would not cover the `sms` SMs (fft_reg.cu);
+// needs c % 16 == 0.
+int launch_irfft2_par(const FftParams& p, int sms, cudaStream_t st);
+bool irfft2_par_narrow(int c, int batch, int sms);
 int fft_reg_prepare();
 int launch_fft_reg(const FftParams& p, bool inverse, cudaStream_t st);
 

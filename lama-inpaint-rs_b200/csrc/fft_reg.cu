@@ -389,20 +389,28 @@ __global__ void __launch_bounds__(256, 2) k_rfft2_pf(const __grid_constant__ Fft
 }
 
 // ------------------------------------------------------------------ irfft2 by row parity (64 x 64)
-// One CTA = one image x 16 channels x one parity h of the output rows: the
+// One CTA = one image x CG channels x one parity h of the output rows: the
 // column pass computes only the outputs y = 2m + h of every inverse column
 // transform (one decimation-in-frequency stage, then 32 points in
-// registers), so the half plane [16][kx][32] fits in shared memory and the
-// row pass stores S with 16 channels = 32 contiguous bytes per pixel and part.
-constexpr int PAR_CG = 16, PAR_KS = 34, PAR_YS = 33;
-constexpr size_t PAR_SMEM = (size_t)PAR_CG * PAR_KS * PAR_YS * sizeof(float2);
+// registers), so the half plane [CG][kx][32] fits in shared memory.
+//   CG = 16, 256 threads (batches): the row pass stores S with 16 channels =
+//     32 contiguous bytes per pixel and part; each thread runs three column
+//     and two row transforms;
+//   CG = 4, 128 threads (small batches, where 16-channel CTAs would leave most
+//     SMs idle): four times the CTAs, one column and one row transform per
+//     thread, 8-byte runs of S.
+constexpr int PAR_KS = 34, PAR_YS = 33;
+template <int CG>
+constexpr size_t par_smem() { return (size_t)CG * PAR_KS * PAR_YS * sizeof(float2); }
 
-__global__ void __launch_bounds__(256, 1) k_irfft2_par(const FftParams p) {
+template <int CG, int NT>
+__global__ void __launch_bounds__(NT, 1) k_irfft2_par(const FftParams p) {
   constexpr int H = 64, W = 64, WH = 33, HALF = 32;
+  constexpr int STEP = NT / CG;  // column slots (and output rows) per pass over the CTA's threads
   extern __shared__ __align__(16) float2 zp[];
   auto P = [&](int c, int kx, int m) -> float2& { return zp[(c * PAR_KS + kx) * PAR_YS + m]; };
-  const int t = threadIdx.x, h = blockIdx.z, b = blockIdx.y, c0 = blockIdx.x * PAR_CG;
-  const int c = t & 15, cc = c0 + c;
+  const int t = threadIdx.x, h = blockIdx.z, b = blockIdx.y, c0 = blockIdx.x * CG;
+  const int c = t % CG, cc = c0 + c;
   const int C2 = 2 * p.c;
   auto ld = [&](int ky, int kx) {
     return __ldg(reinterpret_cast<const float2*>(p.fu + (((size_t)b * H + ky) * WH + kx) * C2 + 2 * cc));
@@ -417,7 +425,7 @@ __global__ void __launch_bounds__(256, 1) k_irfft2_par(const FftParams p) {
     return make_float2(h0.x - hn.y, h0.y + hn.x);
   };
 #pragma unroll 1
-  for (int slot = t >> 4; slot < HALF; slot += 16) {
+  for (int slot = t / CG; slot < HALF; slot += STEP) {
     float2 u[HALF];
     if (slot == 0) {
 #pragma unroll
@@ -447,7 +455,7 @@ __global__ void __launch_bounds__(256, 1) k_irfft2_par(const FftParams p) {
   __syncthreads();
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.s_out);
 #pragma unroll 1
-  for (int m = t >> 4; m < HALF; m += 16) {
+  for (int m = t / CG; m < HALF; m += STEP) {
     const int y = 2 * m + h;
     float2 z[HALF];
 #pragma unroll
@@ -504,11 +512,19 @@ bool fft_pf_supported(int c, int h, int w) { return h == 64 && w == 64 && c % PF
 int fft_pf_prepare() {
   cudaError_t e = cudaFuncSetAttribute(k_rfft2_pf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
   if (e != cudaSuccess) return (int)e;
-  return (int)cudaFuncSetAttribute(k_irfft2_par, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PAR_SMEM);
+  e = cudaFuncSetAttribute(k_irfft2_par<16, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)par_smem<16>());
+  if (e != cudaSuccess) return (int)e;
+  return (int)cudaFuncSetAttribute(k_irfft2_par<4, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)par_smem<4>());
 }
 
-int launch_irfft2_par(const FftParams& p, cudaStream_t st) {
-  k_irfft2_par<<<dim3(p.c / PAR_CG, p.batch, 2), 256, PAR_SMEM, st>>>(p);
+bool irfft2_par_narrow(int c, int batch, int sms) { return c % 4 == 0 && batch * (c / 16) * 2 < sms; }
+
+int launch_irfft2_par(const FftParams& p, int sms, cudaStream_t st) {
+  if (irfft2_par_narrow(p.c, p.batch, sms))
+    k_irfft2_par<4, 128><<<dim3(p.c / 4, p.batch, 2), 128, par_smem<4>(), st>>>(p);
+  else
+    k_irfft2_par<16, 256><<<dim3(p.c / 16, p.batch, 2), 256, par_smem<16>(), st>>>(p);
   return (int)cudaGetLastError();
 }
 

@@ -29,6 +29,7 @@ constexpr int GEMM_MAX_SEGS = 2;
 constexpr int GEMM_MAX_CLASSES = 4;
 constexpr int GEMM_MAX_AMAPS = 3;
 constexpr int GEMM_MAX_GROUPS = 8;
+constexpr int GEMM_MAX_KSPLIT = 8;
 
 enum OutKind : int {
   OUT_SPLIT = 0,     // split bf16 NHWC (optionally halo'd, reflect-filled)
@@ -66,6 +67,13 @@ struct GemmClass {
   int tile0;     // first global tile index of the class
   int ksplit;    // K parts per output tile (split-K; 1 = none)
   int ws_tile0;  // first workspace slice of the class (split-K)
+  // K parts [part0, part0 + nparts) of every output tile run in this launch
+  // (the others in another launch sharing the workspace and counters; the
+  // part that arrives last finishes the tile); part q covers K units
+  // [kcut[q], kcut[q + 1]): 64-wide K blocks, or row-union iterations (one
+  // per group and channel block, in group order) when GemmParams::uni is set
+  int part0, nparts;
+  int16_t kcut[GEMM_MAX_KSPLIT + 1];
   GemmSeg seg[GEMM_MAX_SEGS];
   int ngroup;    // row-union mode: groups of the class's taps
   GemmGroup grp[GEMM_MAX_GROUPS];
@@ -112,9 +120,9 @@ struct GemmParams {
   int out_halo, out_reflect;  // halo width; fill it by reflection
   const void* skip;           // split residual, same geometry as out (may alias it)
   // split-K (classes with ksplit > 1): fp32 partial sums, one [BN][128] slice
-  // per part of each output tile, and one arrival counter per output tile
-  // (indexed by its part-0 slice), zero between launches (the CTA that
-  // finishes a tile resets it)
+  // per part of each output tile (with CTA pairs: of each CTA's 128-pixel
+  // half), and one arrival counter per output tile (indexed by its part-0
+  // slice), zero between launches (the CTA that finishes a tile resets it)
   float* ws;
   int* cnt;
   int* err;                   // device status word (0 = ok)

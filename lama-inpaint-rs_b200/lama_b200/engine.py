@@ -63,6 +63,7 @@ SIGNATURES = [
                                              ctypes.c_int, _vp, _vp]),
     ("lama_set_tiling", ctypes.c_int, [_vp, ctypes.c_int]),
     ("lama_set_spectral_path", ctypes.c_int, [_vp, ctypes.c_int]),
+    ("lama_set_lanes", ctypes.c_int, [_vp, ctypes.c_int]),
     ("lama_debug_wait_timeout", ctypes.c_int, [_vp, ctypes.c_int]),
     ("lama_rfft2_noalloc", ctypes.c_int, [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           _vp, _vp, ctypes.c_char_p, ctypes.c_int]),
@@ -202,6 +203,10 @@ class Engine:
     def set_spectral_path(self, path: int):
         """Spectral-transform kernels for plans built from now on (see include/lama_b200.h)."""
         self._check(lib().lama_set_spectral_path(self._h, path))
+
+    def set_lanes(self, chain_sms: int):
+        """SMs of the spectral graph lane at small batches (0 = one lane, -1 = default)."""
+        self._check(lib().lama_set_lanes(self._h, chain_sms))
 
     def synchronize(self):
         self._check(lib().lama_synchronize(self._h))

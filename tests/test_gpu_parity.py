@@ -307,3 +307,26 @@ def test_prefetching_rfft_matches_the_register_path_over_a_batch(engine_tamed):
     finally:
         engine_tamed.set_spectral_path(engine_tamed.SPECTRAL_AUTO)
     assert np.abs(got - ref).max() <= FLOAT_TOL
+
+
+def test_small_batch_lanes_and_union_pairs_match_the_oracle(engine_tamed, oracle_tamed):
+    """A batch-1 512x512 pass runs its FFC layers on two graph lanes (the
+    spectral chain beside the FFC GEMM's local class and l2g parts, then a
+    tail launch with conv2 that finishes the global class) with CTA-pair
+    row-union tiles and split K; with one lane, and with single-CTA pixel
+    tiles, the pass is the same function: all three against the oracle."""
+    _, _, x = make_input(512, 512, 99)
+    exp = oracle_tamed.forward(x)
+    got = {}
+    try:
+        got["lanes"] = engine_tamed.forward(x)
+        engine_tamed.set_lanes(0)
+        got["one lane"] = engine_tamed.forward(x)
+        engine_tamed.set_tiling(engine_tamed.TILING_PIXEL)
+        got["pixel tiles"] = engine_tamed.forward(x)
+    finally:
+        engine_tamed.set_lanes(-1)
+        engine_tamed.set_tiling(engine_tamed.TILING_AUTO)
+    for k, v in got.items():
+        assert np.abs(v - exp).max() <= FLOAT_TOL, k
+    np.testing.assert_array_equal(got["lanes"], engine_tamed.forward(x))  # deterministic
