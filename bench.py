@@ -465,6 +465,18 @@ def extra_timings(eng, stream):
         st = eng.profile_forward(x.data_ptr(), y.data_ptr(), 1, 512, 512)
         out["b1_512_ops"] = [{"name": s["name"], "launches": s["launches"], "ms": round(s["ms"], 4)} for s in st]
         out["b1_512_eager_ms"] = sum(s["ms"] for s in st)
+        # the same pass as the captured graph runs it (both lanes): per op
+        # class, the exposed time (completion - inputs ready, launch latency
+        # included) and the pass's length
+        tl = eng.profile_timeline(x.data_ptr(), y.data_ptr(), 1, 512, 512)
+        agg = {}
+        for o in tl:
+            k = f"{o['name']}@lane{o['lane']}"
+            a = agg.setdefault(k, [0, 0.0])
+            a[0] += 1
+            a[1] += o["end_ms"] - o["ready_ms"]
+        out["b1_512_graph_ms"] = max(o["end_ms"] for o in tl)
+        out["b1_512_graph_exposed"] = [{"op": k, "launches": n, "ms": round(v, 4)} for k, (n, v) in agg.items()]
     except Exception as ex:
         out["b1_512_ops"] = f"error: {ex}"
     try:

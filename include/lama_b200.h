@@ -125,7 +125,7 @@ int lama_set_spectral_path(lama_engine* e, int path);
 
 /* Graph lanes of small-batch passes (no counterpart in the reference, which
  * runs one launch at a time on the default stream).  Where an FFC layer's
- * GEMM has fewer than two 128 x 128 output tiles per SM (e.g. a batch-1
+ * GEMM has fewer 128 x 128 output tiles than the GPU has SMs (e.g. a batch-1
  * 512x512 pass), the layer's spectral chain (conv1, rfft2, FourierUnit conv,
  * irfft2) runs on `chain_sms` SMs concurrently with the part of the FFC GEMM
  * that does not need it, on the others.  0 = one lane; -1 = the default (40).
@@ -175,6 +175,23 @@ typedef struct {
 
 int lama_profile_forward(lama_engine* e, const float* d_in, int batch, int h, int w, float* d_out,
                          lama_kernel_stat* stats, int max_stats, int* n_stats);
+
+/* Timeline of one forward pass as the captured graph runs it (both lanes):
+ * per launch, in plan order, the time its inputs were ready (the latest
+ * completion of the launches it follows) and its completion, in ms from the
+ * start of the pass, read from timing events recorded inside a copy of the
+ * pass's graph.  end_ms - ready_ms is the launch's exposed time (launch
+ * latency included).  Fills up to `max_ops` records; *n_ops is the number of
+ * launches. */
+typedef struct {
+  char name[32];
+  int lane;        /* graph lane (0, or 1 for the spectral lane of small batches) */
+  float ready_ms;
+  float end_ms;
+} lama_op_time;
+
+int lama_profile_timeline(lama_engine* e, const float* d_in, int batch, int h, int w, float* d_out,
+                          lama_op_time* times, int max_ops, int* n_ops);
 
 /* Diagnostics (used by the layer-by-layer parity tests).
  * lama_debug_run: run only the first `n_ops` launches of the f32 forward plan

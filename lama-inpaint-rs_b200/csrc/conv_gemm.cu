@@ -96,6 +96,18 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t, int 
   return ti;
 }
 
+// The k-th tile of a CTA (pair) slot: from the launch's static schedule when
+// it has one (p.sched: the host's longest-first assignment of tiles of
+// unequal K), else round robin over the slots.  -1 past the slot's last tile.
+__device__ __forceinline__ int tile_of(const GemmParams& p, int slot, int k, int nslots) {
+  if (p.sched) {
+    const int a = __ldg(p.sched_off + slot) + k;
+    return a < __ldg(p.sched_off + slot + 1) ? __ldg(p.sched + a) : -1;
+  }
+  const int t = slot + k * nslots;
+  return t < p.total_tiles ? t : -1;
+}
+
 __device__ __forceinline__ int reflect_idx(int i, int n) {
   if (n == 1) return 0;
   int period = 2 * (n - 1);
@@ -410,7 +422,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int rank = PAIR ? (int)cluster_ctarank() : 0;
-  const int tfirst = PAIR ? blockIdx.x / 2 : blockIdx.x;  // this CTA's (pair's) first tile
+  const int slot = PAIR ? blockIdx.x / 2 : blockIdx.x;  // this CTA's (pair's) slot in the launch's schedule
   const int tstep = PAIR ? gridDim.x / 2 : gridDim.x;
 
   if (threadIdx.x == 0) {
@@ -473,7 +485,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
-        for (int t = tfirst; t < p.total_tiles && ok; t += tstep) {
+        for (int k = 0, t; ok && (t = tile_of(p, slot, k, tstep)) >= 0; k++) {
           const TileInfo ti = decode_tile(p, t, rank);
           const GemmClass& C = p.cls[ti.cls];
           const int wrow = ti.nt * BN + rank * BROWS;
@@ -513,7 +525,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
         uint32_t phase = 0;
         int it = 0;
         bool ok = true;
-        for (int t = tfirst; t < p.total_tiles && ok; t += tstep, it++) {
+        for (int t; ok && (t = tile_of(p, slot, it, tstep)) >= 0; it++) {
           const TileInfo ti = decode_tile(p, t, rank);
           const GemmClass& C = p.cls[ti.cls];
           const int acc = it % NACC;
@@ -583,7 +595,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = tfirst; t < p.total_tiles && ok; t += tstep) {
+      for (int k = 0, t; ok && (t = tile_of(p, slot, k, tstep)) >= 0; k++) {
         const TileInfo ti = decode_tile(p, t, rank);
         const GemmClass& C = p.cls[ti.cls];
         int seg = 0;
@@ -626,7 +638,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = tfirst; t < p.total_tiles && ok; t += tstep, it++) {
+      for (int t; ok && (t = tile_of(p, slot, it, tstep)) >= 0; it++) {
         const TileInfo ti = decode_tile(p, t, rank);
         const int acc = it % NACC;
         if (!mbar_wait(tempty_bar(acc), ((it / NACC) & 1) ^ 1, p.err, 2)) { ok = false; break; }
@@ -674,7 +686,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
     const int quarter = ew & 3, half = ew >> 2;
     const int m = quarter * 32 + lane;
     int it = 0;
-    for (int t = tfirst; t < p.total_tiles; t += tstep, it++) {
+    for (int t; (t = tile_of(p, slot, it, tstep)) >= 0; it++) {
       const TileInfo ti = decode_tile(p, t, rank);
       const GemmClass& C = p.cls[ti.cls];
       const int acc = it % NACC;

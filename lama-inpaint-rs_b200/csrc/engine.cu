@@ -704,13 +704,15 @@ struct Builder {
   void build_ops();  // every launch of the plan's pass, in order
 
   // SMs of the spectral lane for an FFC stack of B images of h x w latents,
-  // or 0 for one lane: small launches (fewer than two 128 x 128 output tiles
-  // of the FFC GEMM per SM) whose latent suits the row-union CTA-pair tiles.
+  // or 0 for one lane: small launches (fewer 128 x 128 output tiles of the
+  // FFC GEMM than SMs) whose latent suits the row-union CTA-pair tiles.
   int lanes_for(int B, int h, int w) const {
     if (e.chain_sms <= 0 || e.tiling != LAMA_TILING_AUTO || e.pair_clusters <= 0) return 0;
     if (w % 32 || h % 4) return 0;
+    // measured: two lanes win at one 512x512 image (3.75 vs 3.91 ms) and lose
+    // at two (5.9 vs 5.1 ms), where the GEMM alone nearly fills the GPU
     const long long outs = (long long)B * ((h * w + 127) / 128) * 4;
-    if (outs >= 2LL * e.sms) return 0;
+    if (outs >= e.sms) return 0;
     return std::min(e.chain_sms, e.sms / 2);
   }
 
@@ -1044,6 +1046,50 @@ struct Builder {
       p.obox_w = std::min(bw, 32);
     }
     op.grid = pair ? 2 * std::min(p.total_tiles, clusters) : std::min(p.total_tiles, sms);
+    // Launches of a few tiles per slot whose tiles differ in K (classes of
+    // different K, split-K parts) get a static longest-first schedule: round
+    // robin would leave some slots with a long tile more than others.
+    {
+      const int nslot = pair ? op.grid / 2 : op.grid;
+      std::vector<int> cost(p.total_tiles);
+      for (int t = 0; t < p.total_tiles; t++) {
+        int c = 0;
+        while (c + 1 < p.nclass && t >= p.cls[c + 1].tile0) c++;
+        const GemmClass& C = p.cls[c];
+        const int part = C.part0 + (t - C.tile0) % C.nparts;
+        int kb = 0;
+        for (int u = C.kcut[part]; u < C.kcut[part + 1]; u++) kb += unit_kb[c][u];
+        cost[t] = kb + 4;  // + the epilogue, about four K blocks' time
+      }
+      bool uneven = p.total_tiles % nslot != 0;
+      for (int t = 1; t < p.total_tiles; t++) uneven = uneven || cost[t] != cost[0];
+      if (uneven && p.total_tiles <= 16 * nslot) {
+        std::vector<int> order(p.total_tiles);
+        for (int t = 0; t < p.total_tiles; t++) order[t] = t;
+        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+        std::vector<long long> load(nslot, 0);
+        std::vector<std::vector<int>> lists(nslot);
+        for (int t : order) {
+          int best = 0;
+          for (int sl = 1; sl < nslot; sl++)
+            if (load[sl] < load[best]) best = sl;
+          load[best] += cost[t];
+          lists[best].push_back(t);
+        }
+        std::vector<int> h_off(nslot + 1, 0), h_sched;
+        for (int sl = 0; sl < nslot; sl++) {
+          h_sched.insert(h_sched.end(), lists[sl].begin(), lists[sl].end());
+          h_off[sl + 1] = (int)h_sched.size();
+        }
+        int* d = (int*)pl.mem.alloc((h_sched.size() + h_off.size()) * sizeof(int), false);
+        if (!pl.mem.dry) {
+          CK(cudaMemcpy(d, h_off.data(), h_off.size() * sizeof(int), cudaMemcpyHostToDevice));
+          CK(cudaMemcpy(d + h_off.size(), h_sched.data(), h_sched.size() * sizeof(int), cudaMemcpyHostToDevice));
+        }
+        p.sched_off = d;
+        p.sched = d + h_off.size();
+      }
+    }
     op.out_ptr = o.p;
     op.out_split = o.kind == OUT_SPLIT;
     op.out_part = o.part;
@@ -1065,6 +1111,8 @@ struct Builder {
     op.flops -= tail_flops;
     tl.g.reset(new GemmParams(p));
     GemmParams& q = *tl.g;
+    q.sched = nullptr;  // one class of equal tiles: round robin
+    q.sched_off = nullptr;
     q.nclass = 1;
     q.cls[0] = p.cls[tail_class];
     q.cls[0].part0 = q.cls[0].ksplit - 1;
@@ -1456,6 +1504,55 @@ std::string human_bytes(double b) {
   return buf;
 }
 
+// Capture a plan's pass into an instantiated CUDA graph: lane 1 forks off the
+// engine stream at its first op and joins back after its last, cross-lane
+// waits become graph edges through events.  With `stamps` (ops + 1 timing
+// events), the graph also records stamps[0] before the first op and
+// stamps[i + 1] after op i on its lane (external event-record nodes), for
+// lama_profile_timeline.
+cudaGraphExec_t capture_plan(lama_engine* e, const Plan& pl, std::vector<cudaEvent_t>* stamps) {
+  cudaGraph_t graph = nullptr;
+  bool two_lanes = false;
+  for (const Op& op : pl.ops) two_lanes = two_lanes || op.lane == 1;
+  EventSet done(two_lanes ? pl.ops.size() + 1 : 0);
+  for (auto& x : done.ev) CK(cudaEventCreateWithFlags(&x, cudaEventDisableTiming));
+  std::vector<char> waited(pl.ops.size(), 0);
+  for (const Op& op : pl.ops)
+    for (int j : op.waits) waited[(size_t)j] = 1;
+  CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  int lerr = 0;
+  const cudaStream_t lane_stream[2] = {e->stream, e->side_stream};
+  if (stamps) lerr = (int)cudaEventRecordWithFlags((*stamps)[0], e->stream, cudaEventRecordExternal);
+  if (two_lanes && !lerr) {  // the side stream joins the capture from the engine stream
+    lerr = (int)cudaEventRecord(done.ev.back(), e->stream);
+    if (!lerr) lerr = (int)cudaStreamWaitEvent(e->side_stream, done.ev.back(), 0);
+  }
+  for (size_t i = 0; i < pl.ops.size() && !lerr; i++) {
+    const Op& op = pl.ops[i];
+    const cudaStream_t st = lane_stream[two_lanes ? op.lane : 0];
+    for (int j : op.waits)
+      if (!lerr && two_lanes) lerr = (int)cudaStreamWaitEvent(st, done.ev[(size_t)j], 0);
+    if (!lerr) lerr = launch_op(op, st);
+    if (!lerr && two_lanes && waited[i]) lerr = (int)cudaEventRecord(done.ev[i], st);
+    if (!lerr && stamps) lerr = (int)cudaEventRecordWithFlags((*stamps)[i + 1], st, cudaEventRecordExternal);
+  }
+  if (two_lanes && !lerr) {  // join: the engine stream waits for the side stream's last op
+    lerr = (int)cudaEventRecord(done.ev.back(), e->side_stream);
+    if (!lerr) lerr = (int)cudaStreamWaitEvent(e->stream, done.ev.back(), 0);
+  }
+  cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
+  if (lerr) {
+    if (graph) cudaGraphDestroy(graph);
+    throw EngineError{LAMA_ECUDA, std::string("kernel launch during capture: ") + cudaGetErrorString((cudaError_t)lerr)};
+  }
+  CK(ce);
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  CK(ie);
+  return exec;
+}
+
 Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int nblocks) {
   auto key = std::make_tuple(kind, B, H, W, h, w, nblocks);
   auto it = e->plans.find(key);
@@ -1478,45 +1575,7 @@ Plan& get_plan(lama_engine* e, int kind, int B, int H, int W, int h, int w, int 
   std::unique_ptr<Plan> pl(new Plan());
   pl->kind = kind; pl->B = B; pl->H = H; pl->W = W; pl->h = h; pl->w = w; pl->nblocks = nblocks;
   build_plan(e, pl.get());
-  // Capture the pass into a CUDA graph: lane 1 forks off the engine stream
-  // at its first op and joins back after its last, cross-lane waits become
-  // graph edges through events.
-  cudaGraph_t graph = nullptr;
-  bool two_lanes = false;
-  for (const Op& op : pl->ops) two_lanes = two_lanes || op.lane == 1;
-  EventSet done(two_lanes ? pl->ops.size() + 1 : 0);
-  for (auto& x : done.ev) CK(cudaEventCreateWithFlags(&x, cudaEventDisableTiming));
-  std::vector<char> waited(pl->ops.size(), 0);
-  for (const Op& op : pl->ops)
-    for (int j : op.waits) waited[(size_t)j] = 1;
-  CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-  int lerr = 0;
-  const cudaStream_t lane_stream[2] = {e->stream, e->side_stream};
-  if (two_lanes) {  // the side stream joins the capture from the engine stream
-    lerr = (int)cudaEventRecord(done.ev.back(), e->stream);
-    if (!lerr) lerr = (int)cudaStreamWaitEvent(e->side_stream, done.ev.back(), 0);
-  }
-  for (size_t i = 0; i < pl->ops.size() && !lerr; i++) {
-    const Op& op = pl->ops[i];
-    const cudaStream_t st = lane_stream[two_lanes ? op.lane : 0];
-    for (int j : op.waits)
-      if (!lerr && two_lanes) lerr = (int)cudaStreamWaitEvent(st, done.ev[(size_t)j], 0);
-    if (!lerr) lerr = launch_op(op, st);
-    if (!lerr && two_lanes && waited[i]) lerr = (int)cudaEventRecord(done.ev[i], st);
-  }
-  if (two_lanes && !lerr) {  // join: the engine stream waits for the side stream's last op
-    lerr = (int)cudaEventRecord(done.ev.back(), e->side_stream);
-    if (!lerr) lerr = (int)cudaStreamWaitEvent(e->stream, done.ev.back(), 0);
-  }
-  cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
-  if (lerr) {
-    if (graph) cudaGraphDestroy(graph);
-    throw EngineError{LAMA_ECUDA, std::string("kernel launch during capture: ") + cudaGetErrorString((cudaError_t)lerr)};
-  }
-  CK(ce);
-  cudaError_t ie = cudaGraphInstantiate(&pl->exec, graph, 0);
-  cudaGraphDestroy(graph);
-  CK(ie);
+  pl->exec = capture_plan(e, *pl, nullptr);
   Plan& ref = *pl;
   e->plans[key] = std::move(pl);
   return ref;
@@ -1944,6 +2003,44 @@ int lama_profile_forward(lama_engine* e, const float* d_in, int batch, int h, in
       n++;
     }
     if (n_stats) *n_stats = n;
+  });
+}
+
+int lama_profile_timeline(lama_engine* e, const float* d_in, int batch, int h, int w, float* d_out,
+                          lama_op_time* times, int max_ops, int* n_ops) {
+  return guarded(e, [&] {
+    if (!d_in || !d_out) throw EngineError{LAMA_EINVAL, "null buffer"};
+    check_shape(batch, h, w, true);
+    Plan& pl = get_plan(e, 0, batch, h, w, h, w, 18);
+    const size_t nin = (size_t)batch * 4 * h * w, nout = (size_t)batch * 3 * h * w;
+    EventSet evs(pl.ops.size() + 1);
+    for (auto& x : evs.ev) CK(cudaEventCreate(&x));
+    cudaGraphExec_t exec = capture_plan(e, pl, &evs.ev);
+    struct ExecGuard {
+      cudaGraphExec_t x;
+      ~ExecGuard() { cudaGraphExecDestroy(x); }
+    } guard{exec};
+    CK(cudaMemcpyAsync(pl.in_f32, d_in, nin * 4, cudaMemcpyDeviceToDevice, e->stream));
+    for (int rep = 0; rep < 2; rep++) CK(cudaGraphLaunch(exec, e->stream));  // the second replay is read
+    CK(cudaMemcpyAsync(d_out, pl.out, nout * 4, cudaMemcpyDeviceToDevice, e->stream));
+    sync_check(e);
+    std::vector<float> end(pl.ops.size(), 0.f);
+    int last[2] = {-1, -1};
+    for (size_t i = 0; i < pl.ops.size(); i++) {
+      const Op& op = pl.ops[i];
+      CK(cudaEventElapsedTime(&end[i], evs.ev[0], evs.ev[i + 1]));
+      float ready = last[op.lane] >= 0 ? end[(size_t)last[op.lane]] : 0.f;
+      for (int j : op.waits) ready = std::max(ready, end[(size_t)j]);
+      last[op.lane] = (int)i;
+      if ((int)i < max_ops && times) {
+        lama_op_time& t = times[i];
+        snprintf(t.name, sizeof(t.name), "%s", op.name.c_str());
+        t.lane = op.lane;
+        t.ready_ms = ready;
+        t.end_ms = end[i];
+      }
+    }
+    if (n_ops) *n_ops = (int)pl.ops.size();
   });
 }
 

@@ -125,6 +125,10 @@ struct GemmParams {
   // slice), zero between launches (the CTA that finishes a tile resets it)
   float* ws;
   int* cnt;
+  // optional static schedule: slot s (a CTA, or a CTA pair) runs tiles
+  // sched[sched_off[s] .. sched_off[s + 1]) in order; null = round robin
+  const int* sched;
+  const int* sched_off;
   int* err;                   // device status word (0 = ok)
 };
 

@@ -43,6 +43,11 @@ class KernelStat(ctypes.Structure):
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
 
 
+class OpTime(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 32), ("lane", ctypes.c_int), ("ready_ms", ctypes.c_float),
+                ("end_ms", ctypes.c_float)]
+
+
 _lib = None
 
 # Every symbol include/lama_b200.h declares: (name, restype, argtypes).
@@ -76,6 +81,8 @@ SIGNATURES = [
                                        ctypes.POINTER(ctypes.c_longlong)]),
     ("lama_profile_forward", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp,
                                             ctypes.POINTER(KernelStat), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    ("lama_profile_timeline", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp,
+                                             ctypes.POINTER(OpTime), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     ("lama_debug_run", ctypes.c_int, [_vp, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     ("lama_debug_read", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p,
                                        ctypes.c_longlong, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p]),
@@ -317,6 +324,15 @@ class Engine:
         self._check(lib().lama_profile_forward(self._h, d_in, batch, h, w, d_out, stats, 64, ctypes.byref(n)))
         return [dict(name=s.name.decode(), launches=s.launches, ms=s.ms, flops=s.flops, bytes=s.bytes)
                 for s in stats[: n.value]]
+
+    def profile_timeline(self, d_in: int, d_out: int, batch: int, h: int, w: int):
+        """Per-launch (name, lane, ready_ms, end_ms) of one graph replay of the forward pass."""
+        cap = 1024
+        ts = (OpTime * cap)()
+        n = ctypes.c_int(0)
+        self._check(lib().lama_profile_timeline(self._h, d_in, batch, h, w, d_out, ts, cap, ctypes.byref(n)))
+        return [dict(name=t.name.decode(), lane=t.lane, ready_ms=t.ready_ms, end_ms=t.end_ms)
+                for t in ts[: min(n.value, cap)]]
 
     # -------------------------------------------------------------- diagnostics
     def debug_run(self, x: np.ndarray, n_ops: int):
