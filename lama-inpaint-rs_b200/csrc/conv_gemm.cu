@@ -27,6 +27,7 @@
 #include <cstdio>
 
 #include "gemm.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace lama {
@@ -405,6 +406,7 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
   static_assert((2 * STAGES + 2 * NACC) * 8 + 12 <= 256, "barriers and TMEM slot fit the 256-byte block");
 
   extern __shared__ uint8_t smem_raw[];
+  pdl_launch_dependents();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * NACC);
@@ -458,6 +460,9 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
   if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // set-up done: from here on the previous kernel's outputs are read (and
+  // buffers it reads are written), so wait for it to complete
+  pdl_wait();
   // epilogue release of an accumulator buffer (pairs: on the even CTA's barrier)
   auto release = [&](int a) {
     tc_fence_before();
@@ -866,24 +871,8 @@ int prepare_bn() {
 
 template <int BN, bool SWAP = false, bool PAIR = false>
 int launch_bn(const GemmParams& p, int grid, cudaStream_t stream) {
-  if constexpr (PAIR) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(384);
-    cfg.dynamicSmemBytes = smem_for<BN, SWAP, PAIR>();
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, k_conv_gemm<BN, SWAP, PAIR>, p);
-  } else {
-    k_conv_gemm<BN, SWAP, PAIR><<<grid, 384, smem_for<BN, SWAP, PAIR>(), stream>>>(p);
-    return (int)cudaGetLastError();
-  }
+  return launch_kernel(k_conv_gemm<BN, SWAP, PAIR>, dim3(grid), dim3(384), smem_for<BN, SWAP, PAIR>(), stream,
+                       PAIR ? 2 : 1, p);
 }
 
 }  // namespace

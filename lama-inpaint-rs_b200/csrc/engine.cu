@@ -35,6 +35,7 @@
 #include "fft.cuh"
 #include "gemm.cuh"
 #include "lama_b200.h"
+#include "launch.cuh"
 #include "outconv.cuh"
 #include "pointwise.cuh"
 #include "ptx.cuh"
@@ -571,6 +572,7 @@ struct Op {
   // one stream in plan order, which respects the same dependencies.
   int lane = 0;
   std::vector<int> waits;
+  bool pdl = false;  // programmatic dependent launch (small passes)
   // output tensor, for the diagnostics entry points: split bf16 or fp32,
   // dims = (B, rows, cols, channels) of the stored layout (halo included;
   // NCHW outputs report (B, C, H, W)).
@@ -580,7 +582,24 @@ struct Op {
   int dims[4] = {0, 0, 0, 0};
 };
 
+}  // namespace
+namespace lama {
+thread_local bool t_pdl_launch = false;
+}
+namespace {
+
+int launch_op_kind(const Op& op, cudaStream_t st);
+
+// A plan's launch; with op.pdl the kernel may start while the previous one on
+// its stream finishes (programmatic dependent launch, launch.cuh).
 int launch_op(const Op& op, cudaStream_t st) {
+  t_pdl_launch = op.pdl;
+  const int r = launch_op_kind(op, st);
+  t_pdl_launch = false;
+  return r;
+}
+
+int launch_op_kind(const Op& op, cudaStream_t st) {
   switch (op.kind) {
     case OP_GEMM: return launch_conv_gemm(*op.g, op.bn, op.grid, st);
     case OP_RFFT: return launch_rfft2(op.f, st);
@@ -647,6 +666,11 @@ void choose_tile(int mh, int mw, int& bh, int& bw, int px = 128, int stride = 1)
 
 // ------------------------------------------------------------------ engine
 constexpr int kDefaultChainSms = 40;
+// convT2 and convT3 run the four phase tiles of each pixel tile on one CTA
+// in a row, so the input rows they share are read from HBM once (measured at
+// 64 images: convT3 4.35 -> 3.93 ms, convT2 1.84 -> 1.81; convT1, whose input
+// is small enough to stay in L2, 1.44 -> 1.54, so it keeps class order)
+constexpr bool kConvTClassGroups = true;
 
 struct Plan {
   int kind = 0;  // 0 f32 forward, 1 u8 inpaint, 2 resblocks, 3 one --sections pass (window)
@@ -752,7 +776,8 @@ struct Builder {
   // class's tiles from the first launch's partial sums.
   void gemm(const std::string& name, const GemmW& Wt, const std::vector<AmapSpec>& amaps,
             const std::vector<ClassSpec>& classes, int cb, int B, int mh, int mw, const OutSpec& o, int relu,
-            int sigmoid, double flops, int max_sms = 0, int tail_class = -1, double tail_flops = 0) {
+            int sigmoid, double flops, int max_sms = 0, int tail_class = -1, double tail_flops = 0,
+            bool class_groups = false) {
     const int sms = max_sms > 0 ? std::min(max_sms, e.sms) : e.sms;
     const int clusters = std::min(e.pair_clusters, sms / 2);
     Op op;
@@ -1063,12 +1088,24 @@ struct Builder {
       }
       bool uneven = p.total_tiles % nslot != 0;
       for (int t = 1; t < p.total_tiles; t++) uneven = uneven || cost[t] != cost[0];
-      if (uneven && p.total_tiles <= 16 * nslot) {
+      bool grouped = class_groups && p.nclass > 1;
+      for (int c = 0; c < p.nclass && grouped; c++)
+        grouped = p.cls[c].nparts == 1 && p.cls[c].ntiles_n == p.cls[0].ntiles_n;
+      std::vector<std::vector<int>> lists;
+      if (grouped) {
+        // every class's tile of one (pixel tile, N tile) on the same slot,
+        // one after another: classes that read the same input rows (the
+        // phases of a transposed convolution) find them in L2
+        lists.assign(nslot, {});
+        const long long ngroups = mt_sched * p.cls[0].ntiles_n;
+        for (long long g = 0; g < ngroups; g++)
+          for (int c = 0; c < p.nclass; c++) lists[(size_t)(g % nslot)].push_back(p.cls[c].tile0 + (int)g);
+      } else if (uneven && p.total_tiles <= 16 * nslot) {
         std::vector<int> order(p.total_tiles);
         for (int t = 0; t < p.total_tiles; t++) order[t] = t;
         std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
         std::vector<long long> load(nslot, 0);
-        std::vector<std::vector<int>> lists(nslot);
+        lists.assign(nslot, {});
         for (int t : order) {
           int best = 0;
           for (int sl = 1; sl < nslot; sl++)
@@ -1076,6 +1113,8 @@ struct Builder {
           load[best] += cost[t];
           lists[best].push_back(t);
         }
+      }
+      if (!lists.empty()) {
         std::vector<int> h_off(nslot + 1, 0), h_sched;
         for (int sl = 0; sl < nslot; sl++) {
           h_sched.insert(h_sched.end(), lists[sl].begin(), lists[sl].end());
@@ -1329,7 +1368,7 @@ struct Builder {
         cls.push_back(c);
       }
       gemm(names[u], e.W.ct[u], {{in, 1, true}}, cls, 64, B, in.H, in.W, split_out(outs[u]), 1, 0,
-           2.0 * B * in.H * in.W * cout * in.C * 9);
+           2.0 * B * in.H * in.W * cout * in.C * 9, 0, -1, 0, kConvTClassGroups && u > 0);
     }
     // OutConv 7x7 64 -> 3 over the reflect-pad-3 halo, + bias, sigmoid -> fp32 NCHW:
     // all 147 tap products of each input row at once, summed in a ring of
@@ -1389,6 +1428,17 @@ void check_device_error(lama_engine* e) {
 void build_plan(lama_engine* e, Plan* pl) {
   Builder b{*e, *pl};
   b.build_ops();
+  // Programmatic dependent launch (a kernel's set-up overlapping the end of
+  // the previous one) is off: measured on one B200 it made the batch-1
+  // 512x512 pass slower (3.71 -> 4.14 ms, graph replay) and a 64-image pass
+  // too (93.2 -> 97.0 ms).  LAMA_PDL=1 turns it on for experiments.
+  {
+    static const bool pdl = [] {
+      const char* v = std::getenv("LAMA_PDL");
+      return v && std::atoi(v) == 1;
+    }();
+    for (Op& op : pl->ops) op.pdl = pdl && op.kind != OP_COPY;
+  }
   // one split-K workspace per lane, sized for its largest GEMM
   size_t wsf[2] = {0, 0};
   int wsc[2] = {0, 0};

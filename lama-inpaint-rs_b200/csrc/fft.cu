@@ -36,6 +36,7 @@
 #include <cstdint>
 
 #include "fft.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace lama {
@@ -246,6 +247,8 @@ __device__ __forceinline__ void load_tw(float2* dst, const float2* src, int n) {
 
 // grid (row-pair blocks of rp, c, b); lines = pairs of rows (a + i b), ls = w + 1
 __global__ void __launch_bounds__(kThreads) k_rows_fwd(const FftParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(16) float2 sm[];
   const int b = blockIdx.z, c = blockIdx.y, y0 = blockIdx.x * 2 * p.rp;
   const int W = p.w, ls = W + 1, R2 = 2 * p.rp;
@@ -304,6 +307,8 @@ __global__ void __launch_bounds__(kThreads) k_rows_fwd(const FftParams p) {
 // grid (kx blocks of kb, channel groups of cg, b); lines = (kx, channel)
 // columns, channel fastest (conflict-free smem reads when storing channel-fastest)
 __global__ void __launch_bounds__(kThreads) k_cols_fwd(const FftParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(16) float2 sm[];
   const int b = blockIdx.z, c0 = blockIdx.y * p.cg, kx0 = blockIdx.x * p.kb;
   const int H = p.h, ls = H + 1, CG = p.cg, nl = CG * p.kb;
@@ -345,6 +350,8 @@ __global__ void __launch_bounds__(kThreads) k_cols_fwd(const FftParams p) {
 // ------------------------------------------------------------------ irfft2
 // grid (kx blocks of kb, channel groups of cg, b); lines = (kx, channel) columns
 __global__ void __launch_bounds__(kThreads) k_cols_inv(const FftParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(16) float2 sm[];
   const int b = blockIdx.z, c0 = blockIdx.y * p.cg, kx0 = blockIdx.x * p.kb;
   const int H = p.h, ls = H + 1, CG = p.cg, nl = CG * p.kb;
@@ -382,6 +389,8 @@ __global__ void __launch_bounds__(kThreads) k_cols_inv(const FftParams p) {
 
 // grid (row-pair blocks of rpi, channel groups of cg, b); lines = (row pair, channel)
 __global__ void __launch_bounds__(kThreads) k_rows_inv(const FftParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(16) float2 sm[];
   const int b = blockIdx.z, c0 = blockIdx.y * p.cg, y0 = blockIdx.x * 2 * p.rpi;
   const int W = p.w, ls = W + 1, fs = W + 1, CG = p.cg, nl = p.rpi * CG;
@@ -574,16 +583,20 @@ int fft_prepare(size_t max_smem) {
 int launch_rfft2(const FftParams& p, cudaStream_t st) {
   const dim3 g0((p.h + 2 * p.rp - 1) / (2 * p.rp), p.c, p.batch);
   const dim3 g1((p.wh + p.kb - 1) / p.kb, (p.c + p.cg - 1) / p.cg, p.batch);
-  k_rows_fwd<<<g0, kThreads, fft_smem_bytes(p, 0), st>>>(p);
-  k_cols_fwd<<<g1, kThreads, fft_smem_bytes(p, 1), st>>>(p);
+  int e = launch_kernel(k_rows_fwd, g0, dim3(kThreads), fft_smem_bytes(p, 0), st, 1, p);
+  if (e) return e;
+  e = launch_kernel(k_cols_fwd, g1, dim3(kThreads), fft_smem_bytes(p, 1), st, 1, p);
+  if (e) return e;
   return (int)cudaGetLastError();
 }
 
 int launch_irfft2(const FftParams& p, cudaStream_t st) {
   const dim3 g1((p.wh + p.kb - 1) / p.kb, (p.c + p.cg - 1) / p.cg, p.batch);
   const dim3 g2((p.h + 2 * p.rpi - 1) / (2 * p.rpi), (p.c + p.cg - 1) / p.cg, p.batch);
-  k_cols_inv<<<g1, kThreads, fft_smem_bytes(p, 1), st>>>(p);
-  k_rows_inv<<<g2, kThreads, fft_smem_bytes(p, 2), st>>>(p);
+  int e = launch_kernel(k_cols_inv, g1, dim3(kThreads), fft_smem_bytes(p, 1), st, 1, p);
+  if (e) return e;
+  e = launch_kernel(k_rows_inv, g2, dim3(kThreads), fft_smem_bytes(p, 2), st, 1, p);
+  if (e) return e;
   return (int)cudaGetLastError();
 }
 

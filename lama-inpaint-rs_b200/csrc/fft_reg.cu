@@ -22,6 +22,7 @@
 #include <cstdint>
 
 #include "fft.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace lama {
@@ -100,6 +101,8 @@ struct Layout {
 // ------------------------------------------------------------------ rfft2
 template <int H, int W>
 __global__ void __launch_bounds__(256) k_rfft2_reg(const FftParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int WH = W / 2 + 1, HALF = W / 2;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const Layout L{reinterpret_cast<float2*>(smem_raw)};
@@ -170,6 +173,8 @@ __global__ void __launch_bounds__(256) k_rfft2_reg(const FftParams p) {
 // ------------------------------------------------------------------ irfft2 (+ feat)
 template <int H, int W>
 __global__ void __launch_bounds__(256) k_irfft2_reg(const FftParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int WH = W / 2 + 1, HALF = W / 2;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const Layout L{reinterpret_cast<float2*>(smem_raw)};
@@ -253,8 +258,8 @@ template <int H, int W>
 int launch_pair(const FftParams& p, bool inverse, cudaStream_t st) {
   const size_t smem = (size_t)CG * KS * YS * sizeof(float2);
   dim3 grid((p.c + CG - 1) / CG, p.batch);
-  if (inverse) k_irfft2_reg<H, W><<<grid, 256, smem, st>>>(p);
-  else k_rfft2_reg<H, W><<<grid, 256, smem, st>>>(p);
+  if (inverse) return launch_kernel(k_irfft2_reg<H, W>, grid, dim3(256), smem, st, 1, p);
+  return launch_kernel(k_rfft2_reg<H, W>, grid, dim3(256), smem, st, 1, p);
   return (int)cudaGetLastError();
 }
 
@@ -287,6 +292,8 @@ static_assert(PF_PLANE >= PF_BUF, "the TMA landing zone fits in the plane buffer
 constexpr size_t PF_SMEM = 1024 + PF_PLANE + 64;
 
 __global__ void __launch_bounds__(256, 2) k_rfft2_pf(const __grid_constant__ FftPfParams q) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int H = 64, W = 64, WH = 33, HALF = 32;
   const FftParams& p = q.p;
   extern __shared__ uint8_t smem_raw[];
@@ -405,6 +412,8 @@ constexpr size_t par_smem() { return (size_t)CG * PAR_KS * PAR_YS * sizeof(float
 
 template <int CG, int NT>
 __global__ void __launch_bounds__(NT, 1) k_irfft2_par(const FftParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int H = 64, W = 64, WH = 33, HALF = 32;
   constexpr int STEP = NT / CG;  // column slots (and output rows) per pass over the CTA's threads
   extern __shared__ __align__(16) float2 zp[];
@@ -522,15 +531,12 @@ bool irfft2_par_narrow(int c, int batch, int sms) { return c % 4 == 0 && batch *
 
 int launch_irfft2_par(const FftParams& p, int sms, cudaStream_t st) {
   if (irfft2_par_narrow(p.c, p.batch, sms))
-    k_irfft2_par<4, 128><<<dim3(p.c / 4, p.batch, 2), 128, par_smem<4>(), st>>>(p);
-  else
-    k_irfft2_par<16, 256><<<dim3(p.c / 16, p.batch, 2), 256, par_smem<16>(), st>>>(p);
-  return (int)cudaGetLastError();
+    return launch_kernel(k_irfft2_par<4, 128>, dim3(p.c / 4, p.batch, 2), dim3(128), par_smem<4>(), st, 1, p);
+  return launch_kernel(k_irfft2_par<16, 256>, dim3(p.c / 16, p.batch, 2), dim3(256), par_smem<16>(), st, 1, p);
 }
 
 int launch_rfft2_pf(const FftPfParams& q, int grid, cudaStream_t st) {
-  k_rfft2_pf<<<grid, 256, PF_SMEM, st>>>(q);
-  return (int)cudaGetLastError();
+  return launch_kernel(k_rfft2_pf, dim3(grid), dim3(256), PF_SMEM, st, 1, q);
 }
 
 

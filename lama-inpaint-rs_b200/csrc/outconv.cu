@@ -27,6 +27,7 @@
 #include <type_traits>
 
 #include "outconv.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace lama {
@@ -45,6 +46,8 @@ constexpr int OC_QCOLS = 26;                 // output columns of a warp (32 inp
 constexpr int OC_STRIP = 4 * OC_QCOLS, OC_SEG_MAX = 64;
 
 __global__ void __launch_bounds__(384, 1) k_outconv_ring(const __grid_constant__ OutConvParams q) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr uint32_t IDESC = idesc_bf16_f32(OC_N);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -331,8 +334,7 @@ void outconv_units(OutConvParams& q, int sms) {
 
 int launch_outconv(const OutConvParams& q, int sms, cudaStream_t st) {
   const int units = q.batch * q.strips * q.segs;
-  k_outconv_ring<<<units < sms ? units : sms, 384, OC_SMEM, st>>>(q);
-  return (int)cudaGetLastError();
+  return launch_kernel(k_outconv_ring, dim3(units < sms ? units : sms), dim3(384), OC_SMEM, st, 1, q);
 }
 
 }  // namespace lama

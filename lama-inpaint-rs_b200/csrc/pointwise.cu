@@ -15,6 +15,7 @@
 #include <cstdint>
 
 #include "pointwise.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace lama {
@@ -49,6 +50,8 @@ __device__ __forceinline__ void input_px_u8(const uint8_t* rgb, const uint8_t* m
 
 template <bool U8>
 __global__ void k_unfold(UnfoldParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   const long long total = (long long)p.batch * (p.H + 6) * p.W;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
@@ -102,6 +105,8 @@ __global__ void k_unfold(UnfoldParams p) {
 
 // fp32 NCHW [B][C][h][w] -> channels [c0, c0+C) of split NHWC [2][B][h+2halo][w+2halo][Ct], reflect halo
 __global__ void k_nchw_to_split(ConvertParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   const long long total = (long long)p.batch * (p.h + 2 * p.halo) * (p.w + 2 * p.halo) * p.c;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
@@ -122,6 +127,8 @@ __global__ void k_nchw_to_split(ConvertParams p) {
 }
 
 __global__ void k_split_to_nchw(ConvertParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   const long long total = (long long)p.batch * p.c * p.h * p.w;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
@@ -143,26 +150,22 @@ inline unsigned blocks_for(long long n, int bs) { return (unsigned)((n + bs - 1)
 
 int launch_unfold_f32(const UnfoldParams& p, cudaStream_t st) {
   const long long n = (long long)p.batch * (p.H + 6) * p.W;
-  k_unfold<false><<<blocks_for(n, 128), 128, 0, st>>>(p);
-  return (int)cudaGetLastError();
+  return launch_kernel(k_unfold<false>, dim3(blocks_for(n, 128)), dim3(128), 0, st, 1, p);
 }
 
 int launch_unfold_u8(const UnfoldParams& p, cudaStream_t st) {
   const long long n = (long long)p.batch * (p.H + 6) * p.W;
-  k_unfold<true><<<blocks_for(n, 128), 128, 0, st>>>(p);
-  return (int)cudaGetLastError();
+  return launch_kernel(k_unfold<true>, dim3(blocks_for(n, 128)), dim3(128), 0, st, 1, p);
 }
 
 int launch_nchw_to_split(const ConvertParams& p, cudaStream_t st) {
   const long long n = (long long)p.batch * (p.h + 2 * p.halo) * (p.w + 2 * p.halo) * p.c;
-  k_nchw_to_split<<<blocks_for(n, 256), 256, 0, st>>>(p);
-  return (int)cudaGetLastError();
+  return launch_kernel(k_nchw_to_split, dim3(blocks_for(n, 256)), dim3(256), 0, st, 1, p);
 }
 
 int launch_split_to_nchw(const ConvertParams& p, cudaStream_t st) {
   const long long n = (long long)p.batch * p.c * p.h * p.w;
-  k_split_to_nchw<<<blocks_for(n, 256), 256, 0, st>>>(p);
-  return (int)cudaGetLastError();
+  return launch_kernel(k_split_to_nchw, dim3(blocks_for(n, 256)), dim3(256), 0, st, 1, p);
 }
 
 }  // namespace lama
