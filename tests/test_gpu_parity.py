@@ -330,3 +330,27 @@ def test_small_batch_lanes_and_union_pairs_match_the_oracle(engine_tamed, oracle
     for k, v in got.items():
         assert np.abs(v - exp).max() <= FLOAT_TOL, k
     np.testing.assert_array_equal(got["lanes"], engine_tamed.forward(x))  # deterministic
+
+
+def test_batched_transforms_at_batch_16_against_float64(engine_tamed):
+    """At 16 images per pass the 64x64 transforms are the persistent
+    TMA-fed rfft2 (walking (image, 4 channels) items) and the 16-channel
+    parity-split irfft2; the spectrum and S = feat + irfft2(fu) of the first
+    resblock against float64 torch for two images of the batch."""
+    from torch_ref import irfft2_ortho, rfft2_ortho
+    base = [make_input(512, 512, s)[2] for s in (111, 112, 113, 114)]
+    xs = np.stack([np.roll(base[i % 4], 17 * (i // 4), axis=1) for i in range(16)])
+    engine_tamed.debug_run(xs, 9)
+    reads = {op: engine_tamed.debug_read(16, 512, 512, op) for op in (5, 6, 7, 8)}
+    assert [reads[op][0] for op in (5, 6, 7, 8)] == ["spectral_conv1", "rfft2", "fourier_conv", "irfft2"]
+    for i in (0, 13):
+        feat = torch.from_numpy(reads[5][1][i].reshape(1, 192, 64, 64)).double()
+        sp = rfft2_ortho(feat)
+        exp_spec = torch.stack((sp.real, sp.imag), -1).permute(0, 2, 3, 1, 4).reshape(64, 33, 384).numpy()
+        got_spec = reads[6][1][i].reshape(64, 33, 384)
+        assert np.abs(got_spec - exp_spec).max() <= 1e-4 * np.abs(exp_spec).max()
+        fu = torch.from_numpy(reads[7][1][i].reshape(1, 64, 33, 192, 2)).double()
+        fc = torch.complex(fu[..., 0], fu[..., 1]).permute(0, 3, 1, 2)
+        exp_s = (feat + irfft2_ortho(fc, 64, 64)).permute(0, 2, 3, 1).numpy()[0]
+        got_s = reads[8][1][i].reshape(64, 64, 192)
+        assert np.abs(got_s - exp_s).max() <= 1e-4 * np.abs(exp_s).max()
