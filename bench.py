@@ -308,9 +308,15 @@ def main():
     clocks.start()
     ms_dev = timed(step_device, args.steps)
     clk = clocks.stop()
-    # correctness guard on the timed outputs: unmasked bytes are the input
-    keep = (mask[:1] == 0)
-    assert torch.equal(out[:1][keep], rgb[:1][keep]), "composite left unmasked pixels modified"
+    # correctness guard on the timed outputs: every image's unmasked bytes are
+    # its input, and the first image's fill is that of a batch-1 pass of the
+    # same pair within one level (batch-1 passes run split-K tiles)
+    keep = (mask == 0).unsqueeze(-1).expand_as(rgb)
+    assert torch.equal(out[keep], rgb[keep]), "composite left unmasked pixels modified"
+    one = torch.empty_like(rgb[:1])
+    eng.inpaint_u8_device(rgb[:1].data_ptr(), mask[:1].data_ptr(), one.data_ptr(), 1, SIZE, SIZE)
+    eng.synchronize()
+    assert (one.int() - out[:1].int()).abs().max().item() <= 1, "a chunk's image differs from its batch-1 pass"
 
     for _ in range(1):
         step_host()
