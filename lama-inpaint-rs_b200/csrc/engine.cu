@@ -666,10 +666,6 @@ void choose_tile(int mh, int mw, int& bh, int& bw, int px = 128, int stride = 1)
 
 // ------------------------------------------------------------------ engine
 constexpr int kDefaultChainSms = 40;
-// Two-lane FFC layers: the global class entirely after the spectral chain
-// (true), or its l2g part beside the chain as split-K parts finished by a
-// conv2 tail launch (false)
-constexpr bool kFfcGlobalAfterChain = false;
 // convT2 and convT3 run the four phase tiles of each pixel tile on one CTA
 // in a row, so the input rows they share are read from HBM once (measured at
 // 64 images: convT3 4.35 -> 3.93 ms, convT2 1.84 -> 1.81; convT1, whose input
@@ -1304,19 +1300,12 @@ struct Builder {
         ClassSpec cgl{1, 128, 384};
         cgl.segs.push_back({0, 0, 128, 1, square_taps(3, 0)});
         cgl.segs.push_back({1, 0, 192, 1, {{0, 0}}});
-        const OutSpec xo = split_out(Xout, sub == 1 ? XA.p : nullptr);
-        if (chain && kFfcGlobalAfterChain) {
-          // the local class beside the spectral chain, the global class after it
-          gemm("ffc_out", F.out, {{Xin, 1, false}}, {cl}, 64, B, h, w, xo, 1, 0, 2.0 * px * 128.0 * 4608,
-               e.sms - chain);
-          gemm("ffc_out", F.out, {{Xin, 1, false}, {S, 1, false}}, {cgl}, 64, B, h, w, xo, 1, 0,
-               2.0 * px * 384.0 * 1344);
-        } else {
-          gemm("ffc_out", F.out, {{Xin, 1, false}, {S, 1, false}}, {cl, cgl}, 64, B, h, w, xo, 1, 0,
-               2.0 * px * (128.0 * 4608 + 384.0 * 1344), chain ? e.sms - chain : 0, chain ? 1 : -1,
-               2.0 * px * 384.0 * 192);
-        }
-        if (chain) pl.ops.back().waits.push_back(i_irfft);  // the last launch reads S
+        // (two lanes: measured faster than running the whole global class
+        // after the chain, 3.73 vs 4.13 ms per batch-1 512x512 pass)
+        gemm("ffc_out", F.out, {{Xin, 1, false}, {S, 1, false}}, {cl, cgl}, 64, B, h, w,
+             split_out(Xout, sub == 1 ? XA.p : nullptr), 1, 0, 2.0 * px * (128.0 * 4608 + 384.0 * 1344),
+             chain ? e.sms - chain : 0, chain ? 1 : -1, 2.0 * px * 384.0 * 192);
+        if (chain) pl.ops.back().waits.push_back(i_irfft);  // the tail launch reads S
         prev0 = (int)pl.ops.size() - 1;
       }
   }
