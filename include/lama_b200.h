@@ -117,10 +117,18 @@ int lama_set_tiling(lama_engine* e, int policy);
  * plane size); LAMA_SPECTRAL_REGISTER runs the register-resident kernels
  * wherever the plane is a power of two with sides 8..64 (two-pass
  * elsewhere); LAMA_SPECTRAL_PREFETCH is REGISTER with the persistent
- * TMA-prefetching rfft2 for 64x64 planes; LAMA_SPECTRAL_AUTO picks by plane
- * size (today the same as PREFETCH).  All paths compute the same function;
- * tests use this to cover each. */
-enum { LAMA_SPECTRAL_AUTO = 0, LAMA_SPECTRAL_TWO_PASS = 1, LAMA_SPECTRAL_REGISTER = 2, LAMA_SPECTRAL_PREFETCH = 3 };
+ * TMA-prefetching rfft2 for 64x64 planes; LAMA_SPECTRAL_TENSOR is PREFETCH
+ * with the rfft2 of 64x64 planes as two DFT GEMMs on the tensor core;
+ * LAMA_SPECTRAL_AUTO picks by plane size and batch (TENSOR for 64x64 planes
+ * at 16 images or more, else PREFETCH).  All paths compute the same
+ * function; tests use this to cover each. */
+enum {
+  LAMA_SPECTRAL_AUTO = 0,
+  LAMA_SPECTRAL_TWO_PASS = 1,
+  LAMA_SPECTRAL_REGISTER = 2,
+  LAMA_SPECTRAL_PREFETCH = 3,
+  LAMA_SPECTRAL_TENSOR = 4
+};
 int lama_set_spectral_path(lama_engine* e, int path);
 
 /* Graph lanes of small-batch passes (no counterpart in the reference, which

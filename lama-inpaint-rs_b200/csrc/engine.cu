@@ -545,7 +545,7 @@ void check_weight_shapes(Weights& loaded) {
 }
 
 // ------------------------------------------------------------------ ops
-enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_IRFFT_PAR, OP_OUTCONV, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_TO_SPLIT, OP_TO_NCHW, OP_COPY };
+enum OpKind { OP_GEMM, OP_RFFT, OP_IRFFT, OP_RFFT_REG, OP_IRFFT_REG, OP_RFFT_PF, OP_RFFT_TC, OP_IRFFT_PAR, OP_OUTCONV, OP_UNFOLD_F32, OP_UNFOLD_U8, OP_TO_SPLIT, OP_TO_NCHW, OP_COPY };
 
 struct Op {
   OpKind kind;
@@ -553,6 +553,7 @@ struct Op {
   int bn = 0, grid = 0;
   std::unique_ptr<GemmParams> g;
   std::unique_ptr<FftPfParams> fpf;
+  std::unique_ptr<FftTcParams> ftc;
   const void* csrc = nullptr;  // OP_COPY: device-to-device copy
   void* cdst = nullptr;
   size_t cbytes = 0;
@@ -607,6 +608,7 @@ int launch_op_kind(const Op& op, cudaStream_t st) {
     case OP_RFFT_REG: return launch_fft_reg(op.f, false, st);
     case OP_IRFFT_REG: return launch_fft_reg(op.f, true, st);
     case OP_RFFT_PF: return launch_rfft2_pf(*op.fpf, op.grid, st);
+    case OP_RFFT_TC: return launch_rfft2_tc(*op.ftc, op.grid, st);
     case OP_IRFFT_PAR: return launch_irfft2_par(op.f, op.grid, st);
     case OP_OUTCONV: return launch_outconv(*op.oc, op.grid, st);
     case OP_UNFOLD_F32: return launch_unfold_f32(op.u, st);
@@ -1228,9 +1230,32 @@ struct Builder {
     const bool reg = fft_reg_supported(h, w) && use_reg_fft();
     if (!reg) fp.tmp = (float2*)pl.mem.alloc(fft_tmp_elems(fp) * sizeof(float2));
     // the prefetching rfft2 beats the register one at batch 1, 8 and 32 (64x64 planes)
-    const bool pf = (e.spectral == LAMA_SPECTRAL_PREFETCH || e.spectral == LAMA_SPECTRAL_AUTO) &&
+    // the tensor-core rfft2 beats the prefetching one from 16 images up (64x64
+    // planes: 8.2 -> 6.0 ms per 64-image pass; 1.8 -> 1.7 ms at 16); at one
+    // image its per-CTA set-up (TMEM, the 80 KB DFT table) makes it slower
+    const bool tc = (e.spectral == LAMA_SPECTRAL_TENSOR || (e.spectral == LAMA_SPECTRAL_AUTO && B >= 16)) &&
+                    fft_tc_supported(192, h, w);
+    const bool pf = (e.spectral == LAMA_SPECTRAL_PREFETCH || e.spectral == LAMA_SPECTRAL_AUTO || tc) &&
                     fft_pf_supported(192, h, w);
-    CUtensorMap feat_map{};
+    CUtensorMap feat_map{}, feat_map_tc{};
+    const void* tc_tab = nullptr;
+    if (tc) {
+      // feat as rows of 64 floats, boxes of 32 floats x 128 rows (2 channels' x-halves)
+      cuuint64_t dims[2] = {64, (cuuint64_t)B * 192 * 64};
+      cuuint64_t strides[1] = {256};
+      cuuint32_t box[2] = {32, 128};
+      cuuint32_t estr[2] = {1, 1};
+      CUresult r = encode_tiled(&feat_map_tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, feat, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS)
+        throw EngineError{LAMA_ECUDA, "cuTensorMapEncodeTiled (feat rows, 128) failed: " + std::to_string((int)r)};
+      std::vector<uint8_t> tab(fft_tc_table_bytes());
+      fft_tc_table(tab.data());
+      void* d = pl.mem.alloc(tab.size(), false);
+      if (!pl.mem.dry) CK(cudaMemcpy(d, tab.data(), tab.size(), cudaMemcpyHostToDevice));
+      tc_tab = d;
+    }
     if (pf) {
       // feat as rows of 64 floats, boxes of 32 floats x 256 rows (4 channels' x-halves)
       cuuint64_t dims[2] = {64, (cuuint64_t)B * 192 * 64};
@@ -1267,10 +1292,13 @@ struct Builder {
              OutSpec{OUT_F32_NCHW, feat, 0, 192, h, w, 0, 0, nullptr}, 1, 0, 2.0 * px * 192 * 384, chain);
         on_lane1(prev0);
         Op r;
-        r.kind = pf ? OP_RFFT_PF : reg ? OP_RFFT_REG : OP_RFFT;
+        r.kind = tc ? OP_RFFT_TC : pf ? OP_RFFT_PF : reg ? OP_RFFT_REG : OP_RFFT;
         r.name = "rfft2";
         r.f = fp;
-        if (pf) {
+        if (tc) {
+          r.ftc.reset(new FftTcParams{feat_map_tc, fp, tc_tab});
+          r.grid = std::min(B * 192 / 4, chain ? chain : e.sms);  // one CTA per SM
+        } else if (pf) {
           r.fpf.reset(new FftPfParams{feat_map, fp});
           r.grid = std::min(B * 192 / 4, 2 * (chain ? chain : e.sms));  // two CTAs per SM
         }
@@ -1727,6 +1755,7 @@ int lama_open(const char* weights_path, int device, lama_engine** out) {
     CKL(fft_prepare(kFftSmem));
     CKL(fft_reg_prepare());
     CKL(fft_pf_prepare());
+    CKL(fft_tc_prepare());
     CKL(outconv_prepare());
     e->d_err = (int*)e->wmem.alloc(256);
     upload_weights(e->W, e->wmem);
@@ -1959,7 +1988,7 @@ int lama_set_lanes(lama_engine* e, int chain_sms) {
 
 int lama_set_spectral_path(lama_engine* e, int path) {
   return guarded(e, [&] {
-    if (path < LAMA_SPECTRAL_AUTO || path > LAMA_SPECTRAL_PREFETCH) throw EngineError{LAMA_EINVAL, "unknown spectral path"};
+    if (path < LAMA_SPECTRAL_AUTO || path > LAMA_SPECTRAL_TENSOR) throw EngineError{LAMA_EINVAL, "unknown spectral path"};
     CK(cudaStreamSynchronize(e->stream));
     e->plans.clear();
     e->spectral = path;

@@ -70,6 +70,20 @@ struct FftPfParams {
   FftParams p;
 };
 
+// The tensor-core rfft2 of 64 x 64 planes (fft_tc.cu): map views feat as rows
+// of 64 floats with boxes of 32 x 128 (two channels' x-halves), 128-byte
+// swizzle; tab is the device copy of fft_tc_table (the two DFT matrices).
+struct FftTcParams {
+  CUtensorMap map;
+  FftParams p;
+  const void* tab;
+};
+bool fft_tc_supported(int c, int h, int w);
+size_t fft_tc_table_bytes();
+void fft_tc_table(uint8_t* out);  // fft_tc_table_bytes() bytes
+int fft_tc_prepare();
+int launch_rfft2_tc(const FftTcParams& q, int grid, cudaStream_t st);
+
 // Two-pass kernels for any plane size (fft.cu).  fft_tiles fills cg/kb/rp/rpi
 // from c, h, w so that every pass fits max_smem (false if none does);
 // pass 0 = rows_fwd, 1 = the column passes, 2 = rows_inv.

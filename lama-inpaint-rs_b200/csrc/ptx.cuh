@@ -77,7 +77,44 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
 }
 
+// Wait without the error short-cut, for draining this CTA's own copies and
+// MMAs on an error path before it exits: at most 2^24 clocks.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > (1ll << 24)) return false;
+  return true;
+}
+
+// ------------------------------------------------------------------ named barriers
+// Barrier `id` (1..15; 0 is __syncthreads) over `n` threads of whole warps.
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("barrier.cta.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+// The same, returning the AND of every participant's `pred` (a group-uniform
+// verdict, e.g. on a bounded wait that only some threads saw run out).
+__device__ __forceinline__ bool named_sync_and(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 // ------------------------------------------------------------------ TMA
+// Plain bulk copy global -> this CTA's shared memory (16-byte aligned
+// addresses, size a multiple of 16), completing on the mbarrier.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

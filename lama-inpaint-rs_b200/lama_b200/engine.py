@@ -205,7 +205,7 @@ class Engine:
         """Tile policy for plans built from now on (see include/lama_b200.h)."""
         self._check(lib().lama_set_tiling(self._h, policy))
 
-    SPECTRAL_AUTO, SPECTRAL_TWO_PASS, SPECTRAL_REGISTER, SPECTRAL_PREFETCH = 0, 1, 2, 3
+    SPECTRAL_AUTO, SPECTRAL_TWO_PASS, SPECTRAL_REGISTER, SPECTRAL_PREFETCH, SPECTRAL_TENSOR = 0, 1, 2, 3, 4
 
     def set_spectral_path(self, path: int):
         """Spectral-transform kernels for plans built from now on (see include/lama_b200.h)."""

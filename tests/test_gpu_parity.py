@@ -354,3 +354,35 @@ def test_batched_transforms_at_batch_16_against_float64(engine_tamed):
         exp_s = (feat + irfft2_ortho(fc, 64, 64)).permute(0, 2, 3, 1).numpy()[0]
         got_s = reads[8][1][i].reshape(64, 64, 192)
         assert np.abs(got_s - exp_s).max() <= 1e-4 * np.abs(exp_s).max()
+
+
+def test_tensor_core_rfft_against_float64_over_a_batch(engine_tamed, oracle_tamed):
+    """The tensor-core rfft2 (two split-BF16 DFT GEMMs per (image, 4 channels)
+    item, one persistent CTA per SM walking 768 items at 16 images): the
+    spectrum of the first resblock against float64 torch on the engine's own
+    conv1 output, and S = feat + irfft2(fu) after it, for two images of the
+    batch; and a single-image pass with it against the oracle."""
+    from torch_ref import irfft2_ortho, rfft2_ortho
+    base = [make_input(512, 512, s)[2] for s in (121, 122, 123, 124)]
+    xs = np.stack([np.roll(base[i % 4], 23 * (i // 4), axis=2) for i in range(16)])
+    try:
+        engine_tamed.set_spectral_path(engine_tamed.SPECTRAL_TENSOR)
+        engine_tamed.debug_run(xs, 9)
+        reads = {op: engine_tamed.debug_read(16, 512, 512, op) for op in (5, 6, 7, 8)}
+        _, _, x = make_input(512, 512, 125)
+        single = engine_tamed.forward(x)
+    finally:
+        engine_tamed.set_spectral_path(engine_tamed.SPECTRAL_AUTO)
+    assert [reads[op][0] for op in (5, 6, 7, 8)] == ["spectral_conv1", "rfft2", "fourier_conv", "irfft2"]
+    for i in (0, 13):
+        feat = torch.from_numpy(reads[5][1][i].reshape(1, 192, 64, 64)).double()
+        sp = rfft2_ortho(feat)
+        exp_spec = torch.stack((sp.real, sp.imag), -1).permute(0, 2, 3, 1, 4).reshape(64, 33, 384).numpy()
+        got_spec = reads[6][1][i].reshape(64, 33, 384)
+        assert np.abs(got_spec - exp_spec).max() <= 1e-4 * np.abs(exp_spec).max(), i
+        fu = torch.from_numpy(reads[7][1][i].reshape(1, 64, 33, 192, 2)).double()
+        fc = torch.complex(fu[..., 0], fu[..., 1]).permute(0, 3, 1, 2)
+        exp_s = (feat + irfft2_ortho(fc, 64, 64)).permute(0, 2, 3, 1).numpy()[0]
+        got_s = reads[8][1][i].reshape(64, 64, 192)
+        assert np.abs(got_s - exp_s).max() <= 1e-4 * np.abs(exp_s).max(), i
+    assert np.abs(single - oracle_tamed.forward(x)).max() <= FLOAT_TOL
