@@ -2,7 +2,7 @@
 the CPU oracle (a restatement of lama-rs/src/cpu.rs).
 
 * the bench's pass: one lama_inpaint_u8_device chunk of 64 pairs at 512x512
-  (CTA-pair GEMM tiles, the persistent rfft2 walking ~10 (image, channel
+  (CTA-pair GEMM tiles, the tensor-core rfft2 walking ~21 (image, channel
   group) items per CTA, the parity-split irfft2, the composite fused into the
   OutConv), two images against the oracle composite and every image against
   a batch-1 call;

@@ -333,10 +333,10 @@ def test_small_batch_lanes_and_union_pairs_match_the_oracle(engine_tamed, oracle
 
 
 def test_batched_transforms_at_batch_16_against_float64(engine_tamed):
-    """At 16 images per pass the 64x64 transforms are the persistent
-    TMA-fed rfft2 (walking (image, 4 channels) items) and the 16-channel
-    parity-split irfft2; the spectrum and S = feat + irfft2(fu) of the first
-    resblock against float64 torch for two images of the batch."""
+    """At 16 images per pass the automatic path runs the 64x64 transforms as
+    the tensor-core rfft2 (walking (image, 4 channels) items) and the
+    16-channel parity-split irfft2; the spectrum and S = feat + irfft2(fu) of
+    the first resblock against float64 torch for two images of the batch."""
     from torch_ref import irfft2_ortho, rfft2_ortho
     base = [make_input(512, 512, s)[2] for s in (111, 112, 113, 114)]
     xs = np.stack([np.roll(base[i % 4], 17 * (i // 4), axis=1) for i in range(16)])
