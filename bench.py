@@ -397,7 +397,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_dev / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 I/O; convolutions as three bf16 tensor-core products of split operands (fp32 "
-                     "accumulation), activations stored as bf16 hi/lo pairs (16 significant bits); fp32 FFTs",
+                     "accumulation), activations stored as bf16 hi/lo pairs (16 significant bits); fp32 irfft2, "
+                     "rfft2 as split-bf16 DFT GEMMs (fp32 accumulation)",
             "data": "synthetic: seeded value-noise images + brush masks (8 distinct pairs cycled), seeded BASELINE init",
             "config": {"workload": "config 4: 256 x 512x512 pairs partitioned round-robin over N GPUs, "
                                    "weights replicated",
