@@ -556,15 +556,20 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
                 constexpr int KS = decltype(kst)::value;
                 constexpr uint32_t SBO = KS == 4 ? 1024u : 512u, LAYOUT = KS == 4 ? 2u : 4u;
                 constexpr int TPK = KS == 4 ? 1 : 2;  // taps per K block
+                // descriptors of the stage's first A row and first B block; the
+                // others differ only in the start-address field (bytes / 16,
+                // shared-memory addresses stay below 2^18 so it never carries)
+                const uint64_t a0 = smem_desc(sa, SBO, LAYOUT), b0 = smem_desc(sa + U_A, 1024u, 2u);
+                const uint64_t dap = apart >> 4;
                 for (int j = 0; j < G.ndy; j++) {
-                  const uint32_t aj = sa + (uint32_t)j * rowb;
-                  const uint32_t bj = sa + U_A + (uint32_t)(j / TPK) * 2u * B_PART + (uint32_t)(j % TPK) * 64u;
+                  const uint64_t aj = a0 + (((uint32_t)j * rowb) >> 4);
+                  const uint64_t bj = b0 + (((uint32_t)(j / TPK) * 2u * B_PART + (uint32_t)(j % TPK) * 64u) >> 4);
 #pragma unroll
                   for (int k = 0; k < KS; k++) {
-                    const uint64_t a_hi = smem_desc(aj + k * 32, SBO, LAYOUT);
-                    const uint64_t a_lo = smem_desc(aj + apart + k * 32, SBO, LAYOUT);
-                    const uint64_t b_hi = smem_desc(bj + k * 32, 1024u, 2u);
-                    const uint64_t b_lo = smem_desc(bj + B_PART + k * 32, 1024u, 2u);
+                    const uint64_t a_hi = aj + 2u * k;
+                    const uint64_t a_lo = a_hi + dap;
+                    const uint64_t b_hi = bj + 2u * k;
+                    const uint64_t b_lo = b_hi + (B_PART >> 4);
                     if constexpr (PAIR) {
                       mma_bf16_pair(d_tmem, a_lo, b_hi, IDESC, accum);
                       mma_bf16_pair(d_tmem, a_hi, b_lo, IDESC, 1u);
@@ -654,16 +659,18 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
           tc_fence_after();
           const uint32_t sa = smem0 + (uint32_t)stage * STAGE;
           const uint32_t sb = sa + 2 * A_PART;
+          // as in the row-union loop: only the start-address fields differ
+          const uint64_t a0 = smem_desc(sa, a_sbo, a_layout), b0 = smem_desc(sb, 1024u, 2u);
+          const uint64_t dal = (sw64 ? 8192u : A_PART) >> 4;
 #pragma unroll
           for (int k = 0; k < 4; k++) {
             // 64-byte swizzle (32-channel sub-boxes): [sub][part][128 px][32 ch];
             // 128-byte swizzle: [part][128 px][64 ch]
             const uint32_t aoff = sw64 ? (uint32_t)((k >> 1) * 16384 + (k & 1) * 32) : (uint32_t)(k * 32);
-            const uint32_t alo = sw64 ? 8192u : A_PART;
-            const uint64_t a_hi = smem_desc(sa + aoff, a_sbo, a_layout);
-            const uint64_t a_lo = smem_desc(sa + alo + aoff, a_sbo, a_layout);
-            const uint64_t b_hi = smem_desc(sb + k * 32, 1024u, 2u);
-            const uint64_t b_lo = smem_desc(sb + B_PART + k * 32, 1024u, 2u);
+            const uint64_t a_hi = a0 + (aoff >> 4);
+            const uint64_t a_lo = a_hi + dal;
+            const uint64_t b_hi = b0 + 2u * k;
+            const uint64_t b_lo = b_hi + (B_PART >> 4);
             if constexpr (PAIR) {
               mma_bf16_pair(d_tmem, a_lo, b_hi, IDESC, (kb != ti.kb0 || k != 0) ? 1u : 0u);
               mma_bf16_pair(d_tmem, a_hi, b_lo, IDESC, 1u);
