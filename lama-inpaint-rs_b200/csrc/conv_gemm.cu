@@ -552,8 +552,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
               const uint32_t sa = smem0 + (uint32_t)stage * 2u * STAGE;
               // the K steps of one tap: 64-channel rows (128-byte swizzle) or
               // 32-channel rows (64-byte swizzle), unrolled per case
-              auto tap_mmas = [&](auto kst) {
-                constexpr int KS = decltype(kst)::value;
+              auto tap_mmas = [&](auto kst, auto ndy) {
+                constexpr int KS = decltype(kst)::value, NDY = decltype(ndy)::value;
                 constexpr uint32_t SBO = KS == 4 ? 1024u : 512u, LAYOUT = KS == 4 ? 2u : 4u;
                 constexpr int TPK = KS == 4 ? 1 : 2;  // taps per K block
                 // descriptors of the stage's first A row and first B block; the
@@ -561,7 +561,8 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
                 // shared-memory addresses stay below 2^18 so it never carries)
                 const uint64_t a0 = smem_desc(sa, SBO, LAYOUT), b0 = smem_desc(sa + U_A, 1024u, 2u);
                 const uint64_t dap = apart >> 4;
-                for (int j = 0; j < G.ndy; j++) {
+#pragma unroll
+                for (int j = 0; j < NDY; j++) {
                   const uint64_t aj = a0 + (((uint32_t)j * rowb) >> 4);
                   const uint64_t bj = b0 + (((uint32_t)(j / TPK) * 2u * B_PART + (uint32_t)(j % TPK) * 64u) >> 4);
 #pragma unroll
@@ -583,8 +584,17 @@ __global__ void __launch_bounds__(384, 1) k_conv_gemm(const __grid_constant__ Ge
                   }
                 }
               };
-              if (sw64) tap_mmas(std::integral_constant<int, 2>{});
-              else tap_mmas(std::integral_constant<int, 4>{});
+              // the group's taps as a compile-time count (whole loops unrolled)
+              auto by_ndy = [&](auto kst) {
+                switch (G.ndy) {
+                  case 1: tap_mmas(kst, std::integral_constant<int, 1>{}); break;
+                  case 2: tap_mmas(kst, std::integral_constant<int, 2>{}); break;
+                  case 3: tap_mmas(kst, std::integral_constant<int, 3>{}); break;
+                  default: tap_mmas(kst, std::integral_constant<int, 4>{}); break;
+                }
+              };
+              if (sw64) by_ndy(std::integral_constant<int, 2>{});
+              else by_ndy(std::integral_constant<int, 4>{});
               if constexpr (PAIR) mma_commit_pair(empty_bar(stage), 3);
               else mma_commit(empty_bar(stage));
               if (++stage == USTAGES) { stage = 0; phase ^= 1; }
