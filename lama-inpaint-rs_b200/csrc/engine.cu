@@ -1256,7 +1256,7 @@ struct Builder {
       if (!pl.mem.dry) CK(cudaMemcpy(d, tab.data(), tab.size(), cudaMemcpyHostToDevice));
       tc_tab = d;
     }
-    if (pf) {
+    if (pf && !tc) {
       // feat as rows of 64 floats, boxes of 32 floats x 256 rows (4 channels' x-halves)
       cuuint64_t dims[2] = {64, (cuuint64_t)B * 192 * 64};
       cuuint64_t strides[1] = {256};
