@@ -120,7 +120,7 @@ int lama_set_tiling(lama_engine* e, int policy);
  * TMA-prefetching rfft2 for 64x64 planes; LAMA_SPECTRAL_TENSOR is PREFETCH
  * with the rfft2 of 64x64 planes as two DFT GEMMs on the tensor core;
  * LAMA_SPECTRAL_AUTO picks by plane size and batch (TENSOR for 64x64 planes
- * at 16 images or more, else PREFETCH).  All paths compute the same
+ * at 8 images or more, else PREFETCH).  All paths compute the same
  * function; tests use this to cover each. */
 enum {
   LAMA_SPECTRAL_AUTO = 0,

@@ -1230,10 +1230,11 @@ struct Builder {
     const bool reg = fft_reg_supported(h, w) && use_reg_fft();
     if (!reg) fp.tmp = (float2*)pl.mem.alloc(fft_tmp_elems(fp) * sizeof(float2));
     // the prefetching rfft2 beats the register one at batch 1, 8 and 32 (64x64 planes)
-    // the tensor-core rfft2 beats the prefetching one from 16 images up (64x64
-    // planes: 8.2 -> 6.0 ms per 64-image pass; 1.8 -> 1.7 ms at 16); at one
-    // image its per-CTA set-up (TMEM, the 80 KB DFT table) makes it slower
-    const bool tc = (e.spectral == LAMA_SPECTRAL_TENSOR || (e.spectral == LAMA_SPECTRAL_AUTO && B >= 16)) &&
+    // the tensor-core rfft2 beats the prefetching one from 8 images up (64x64
+    // planes, per pass of 36 launches: 8.2 -> 6.0 ms at 64 images, 1.8 -> 1.7
+    // at 16, 1.07 -> 1.05 at 8); below that its per-CTA set-up (TMEM, the 80 KB
+    // DFT table) makes it slower (0.75 -> 0.83 ms at 4, 0.55 -> 0.79 at 1)
+    const bool tc = (e.spectral == LAMA_SPECTRAL_TENSOR || (e.spectral == LAMA_SPECTRAL_AUTO && B >= 8)) &&
                     fft_tc_supported(192, h, w);
     const bool pf = (e.spectral == LAMA_SPECTRAL_PREFETCH || e.spectral == LAMA_SPECTRAL_AUTO || tc) &&
                     fft_pf_supported(192, h, w);
